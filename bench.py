@@ -1,0 +1,394 @@
+#!/usr/bin/env python
+"""Benchmark of one sparse global-attention layer (the hot path) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg2] [--shard qblocks|heads] [--kernel auto]
+
+A step is one pass of the hot path over one layer of synthetic input:
+block-mask estimator on the sparse heads + one block-sparse attention launch
+(sparse heads through their masks, dense-profiled heads through the dense path
+of the same kernel).  Default workload: config 2 (32 frames, 43,968 tokens,
+16 heads x 64, mass 0.9, heads 0-3 dense).  With N > 1 ranks (torchrun, one
+process per GPU, NCCL) the layer's query blocks (or heads) are split across
+ranks: total work is fixed ("strong"), no collective is needed inside the
+layer because every rank holds the full K/V of the layer.
+
+Prints ONE JSON line on rank 0.  ``value`` is ms per layer (max over ranks).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "sparse-attention-vggt_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "ms per sparse global-attn layer & kept-block TFLOPS at 32/100 frames; frames/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", default="cfg2")
+    p.add_argument("--shard", choices=("qblocks", "heads"), default="qblocks")
+    p.add_argument("--kernel", default="auto")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample-blocks", type=int, default=48)
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 0.0)),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS)
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def reduce_max(x, world):
+    if world == 1:
+        return float(x)
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def reduce_sum(x, world):
+    if world == 1:
+        return float(x)
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.path = None
+        self.device_index = device_index
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            bus = None
+            try:
+                pr = torch.cuda.get_device_properties(self.device_index)
+                bus = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            except Exception:
+                pass
+            cmd = ["nvidia-smi", "--query-gpu=" + self.QUERY, "--format=csv,noheader,nounits",
+                   "-lms", "50"]
+            if bus:
+                cmd += ["--id=" + bus]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def shard_inputs(x, cfg, rank, world, shard, device):
+    """Per-rank slice of the layer.  qblocks: contiguous query-block range,
+    all heads; heads: contiguous head range, all tokens."""
+    if world == 1:
+        return x.q, x.kp, x.vp, x.ks, x.vs, list(cfg.dense_heads), (0, x.shape.n_tokens)
+    if shard == "qblocks":
+        qbc = x.shape.n_qblocks
+        per = math.ceil(qbc / world)
+        b0, b1 = rank * per, min(qbc, (rank + 1) * per)
+        r0, r1 = b0 * cfg.block, min(x.shape.n_tokens, b1 * cfg.block)
+        q = x.q[:, r0:r1].contiguous()
+        return q, x.kp, x.vp, x.ks, x.vs, list(cfg.dense_heads), (r0, r1)
+    h = cfg.heads
+    per = math.ceil(h / world)
+    h0, h1 = rank * per, min(h, (rank + 1) * per)
+    sl = slice(h0, h1)
+    dense = [d - h0 for d in cfg.dense_heads if h0 <= d < h1]
+    return (x.q[sl].contiguous(), x.kp[sl].contiguous(), x.vp[sl].contiguous(),
+            x.ks[sl].contiguous(), x.vs[sl].contiguous(), dense, (0, x.shape.n_tokens))
+
+
+def cpu_baseline(cfg, x_cpu, sample_blocks):
+    """The reference's CPU PyTorch path (restated in oracle.cpu_path) on a
+    bounded sample of query blocks, extrapolated to ms per full layer."""
+    from oracle import cpu_path
+    shape = x_cpu.shape
+    qbc = shape.n_qblocks
+    nsample = min(sample_blocks, qbc)
+    qblocks = sorted(set(int(round(i * (qbc - 1) / max(nsample - 1, 1))) for i in range(nsample)))
+    scale = cfg.dim ** -0.5
+    if cfg.mode == "topk":
+        from oracle import topk_budget
+        budget = topk_budget(cfg.retention, shape.n_tokens, shape.n_special, shape.n_blocks,
+                             cfg.block)
+    else:
+        budget = cfg.tau
+    q, kp, vp, ks, vs = (t.float() for t in (x_cpu.q, x_cpu.kp, x_cpu.vp, x_cpu.ks, x_cpu.vs))
+    t0 = time.perf_counter()
+    cpu_path.block_mean(q, cfg.block)
+    cpu_path.block_mean(kp, cfg.block)
+    t_pool = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    cpu_path.layer_sample(q, kp, vp, ks, vs, mode=cfg.mode, budget=budget,
+                          dense_heads=cfg.dense_heads, qblocks=qblocks, scale=scale,
+                          block=cfg.block)
+    t_sample = time.perf_counter() - t0
+    per_block = max(t_sample - t_pool, 0.0) / len(qblocks)
+    ms = (t_pool + per_block * qbc) * 1e3
+    return {"value": ms, "unit": "ms/layer", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": "%d of %d query blocks x 16 heads of %s (estimator pooling over the full "
+                      "layer), torch fp32 CPU, extrapolated linearly; %.1f s measured"
+                      % (len(qblocks), qbc, cfg.name, t_pool + t_sample)}
+
+
+def workload_desc(cfg, shape):
+    rule = ("top-k %g%% of key blocks" % (cfg.retention * 100) if cfg.mode == "topk"
+            else "softmax-mass threshold %g" % cfg.tau)
+    dense = ("heads %s dense" % ",".join(map(str, cfg.dense_heads))) if cfg.dense_heads else \
+        "all heads sparse"
+    return ("%s: one sparse global-attention layer, %d frames x 1374 tokens = %d tokens, "
+            "16 heads x 64, 64x64 blocks, %s, %s; estimator + block-sparse attention"
+            % (cfg.name, cfg.frames, shape.n_tokens, rule, dense))
+
+
+def run_reference_arm(args, rank, world):
+    from vggt_sparse.configs import CONFIGS
+    from vggt_sparse.synthetic import clustered_layer
+    cfg = CONFIGS[args.config]
+    if rank != 0:
+        return
+    x = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device="cpu",
+                        dtype=torch.bfloat16)
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = max(4, args.cpu_sample_blocks // 4)
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, x, 2)
+    vals = [cpu_baseline(cfg, x, sample) for _ in range(args.steps)]
+    ms = statistics.median(v["value"] for v in vals)
+    cb = dict(vals[0])
+    cb["value"] = ms
+    line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": workload_desc(cfg, x.shape), "frames": cfg.frames,
+                       "tokens": x.shape.n_tokens, "heads": 16, "head_dim": 64},
+            "cpu_baseline": cb,
+            "e2e": {"value": ms, "unit": "ms/layer", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    import vggt_sparse
+    from vggt_sparse.configs import CONFIGS
+    from vggt_sparse.synthetic import clustered_layer
+    cfg = CONFIGS[args.config]
+    device = torch.device("cuda", torch.cuda.current_device())
+    x = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device=device,
+                        dtype=torch.bfloat16)
+    q, kp, vp, ks, vs, dense, rows = shard_inputs(x, cfg, rank, world, args.shard, device)
+    heads = q.shape[0]
+    layer = vggt_sparse.SparseGlobalLayer(heads, mode=cfg.mode, retention=cfg.retention,
+                                          tau=cfg.tau, dense_heads=dense, block=cfg.block,
+                                          kernel=args.kernel)
+    if cfg.mode == "topk":
+        # the budget follows the FULL layer size, as the reference computes it
+        layer.topk = vggt_sparse.topk_budget(cfg.retention, x.shape.n_tokens, x.shape.n_special,
+                                             x.shape.n_blocks, cfg.block)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
+    launches_per_step = (3 if layer.sparse_heads else 0) + 1
+
+    for _ in range(args.warmup):
+        layer(q, kp, vp, ks, vs, out=out)
+    torch.cuda.synchronize()
+    flops_local = layer.kept_flops(q.shape[1], kp.shape[1], ks.shape[1], q.shape[2])
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(device.index) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    for i in range(args.steps):
+        flush.zero_()
+        layer(q, kp, vp, ks, vs, out=out, events=ev[i])
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
+    est_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    att_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    ms_local = sum(step_ms) / len(step_ms)
+    ms = reduce_max(ms_local, world)
+    att_local = sum(att_ms) / len(att_ms)
+    est_local = sum(est_ms) / len(est_ms)
+    flops_total = reduce_sum(flops_local, world)
+
+    # end-to-end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = [t.cpu().pin_memory() for t in (q, kp, vp, ks, vs)]
+        dev_in = [torch.empty_like(t) for t in (q, kp, vp, ks, vs)]
+        host_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        d2h = host_out.numel() * host_out.element_size()
+        for _ in range(max(1, args.warmup // 2)):
+            for d_, h_ in zip(dev_in, host):
+                d_.copy_(h_, non_blocking=True)
+            o = layer(*dev_in)
+            host_out.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+        e2e_steps = max(3, args.steps // 5)
+        barrier(world)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(e2e_steps):
+            for d_, h_ in zip(dev_in, host):
+                d_.copy_(h_, non_blocking=True)
+            o = layer(*dev_in)
+            host_out.copy_(o, non_blocking=True)
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = reduce_max(s0.elapsed_time(s1) / e2e_steps, world)
+        e2e = {"value": e2e_ms, "unit": "ms/layer", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+               "path": "host pinned q/k_patch/v_patch/k_special/v_special -> "
+                       "vggt_sparse.SparseGlobalLayer -> host out"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        x_cpu = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device="cpu",
+                                dtype=torch.bfloat16)
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu = cpu_baseline(cfg, x_cpu, args.cpu_sample_blocks)
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    peaks = load_peaks()
+    att_tflops = flops_local / (att_local * 1e-3) / 1e12
+    n_sparse = len(layer.sparse_heads)
+    qbc = math.ceil(q.shape[1] / cfg.block)
+    idx, cnt = layer.last_masks
+    est_bytes = (n_sparse * (q.shape[1] + kp.shape[1]) * q.shape[2] * 2 +
+                 idx.numel() * 4 + cnt.numel() * 4)
+    line = {
+        "metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload_desc(cfg, x.shape), "frames": cfg.frames,
+                   "tokens": x.shape.n_tokens, "heads": 16, "head_dim": 64,
+                   "selection": cfg.mode, "dense_heads": list(cfg.dense_heads),
+                   "parallelism": ("%s-sharded x%d" % (args.shard, world)) if world > 1
+                   else "single GPU",
+                   "l2": "inputs 270 MB > 126 MB L2; 256 MB flush write between timed steps "
+                         "(outside the per-step events)",
+                   "kernel": args.kernel},
+        "kept_block_tflops": flops_total / (ms * 1e-3) / 1e12,
+        "kept_block_gflop_per_layer": flops_total / 1e9,
+        "frames_per_s": cfg.frames / (ms * 1e-3),
+        "estimator_ms": est_local, "attention_ms": att_local,
+        "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
+                     "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": att_tflops / peaks["bf16_tflops"], "traffic": None,
+                     "flops_per_launch": flops_local,
+                     "peak_source": peaks["source"] + " bf16 burst"},
+        "estimator_roofline": {"bound": "hbm", "achieved": est_bytes / (est_local * 1e-3) / 1e9,
+                               "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": est_bytes / (est_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                               "bytes_per_step": est_bytes,
+                               "peak_source": peaks["source"]},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+/*
+ * vggt_sparse.h — C ABI of the B200 (sm_100a) block-sparse global attention
+ * used inside VGGT-style global-attention blocks.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), enqueues work on that stream, never synchronises and
+ * never allocates: scratch buffers are caller-provided.  Return value 0 means
+ * the work was enqueued; a negative value is an argument error (the message is
+ * available from vggt_sparse_last_error()); a positive value is a CUDA error
+ * code from the launch.
+ *
+ * Tensor layouts follow the reference operator
+ * (saf3r/triton/adaptive_block_attention.py:63-83):
+ *   q        [heads, n_tokens,  dim]   bf16 or fp16, contiguous
+ *   patch_k  [heads, n_patch,   dim]   same dtype (patch tokens only)
+ *   patch_v  [heads, n_patch,   dim]
+ *   special_k[heads, n_special, dim]   camera + register tokens, always attended
+ *   special_v[heads, n_special, dim]
+ *   indices  [n_slots, ceil(n_tokens/block_q), max_blocks] int32, ascending
+ *            unique patch-block ids; only the first `count` slots are read
+ *   counts   [n_slots] int32 (reference) or [n_slots, n_qblocks] int32
+ *   head_ids [n_slots] int32, the real head served by each slot
+ *
+ * Device-side validation: an index outside [0, ceil(n_patch/block_k)) or a
+ * count outside [0, max_blocks] is never dereferenced; the kernel skips it and
+ * ORs a VGGT_STATUS_* bit into *status (when status is non-NULL).
+ */
+#ifndef VGGT_SPARSE_H
+#define VGGT_SPARSE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define VGGT_DTYPE_BF16 0
+#define VGGT_DTYPE_FP16 1
+
+/* selection modes of the block-mask estimator */
+#define VGGT_SELECT_TOPK 0 /* k highest pooled scores, ties -> lower block id */
+#define VGGT_SELECT_MASS 1 /* smallest prefix of the descending order whose softmax mass reaches tau */
+
+/* attention kernel families */
+#define VGGT_ATTN_AUTO 0    /* tcgen05 when the shape is supported, else the mma.sync kernel */
+#define VGGT_ATTN_MMA_SYNC 1 /* warp-level mma.sync tiles, one CTA per (query block, slot) */
+#define VGGT_ATTN_TCGEN05 2  /* TMA + tcgen05/TMEM kernel, 128-row tiles */
+
+/* device status bits (ORed into *status) */
+#define VGGT_STATUS_BAD_INDEX 1 /* a selected block id was outside [0, n_blocks) */
+#define VGGT_STATUS_BAD_COUNT 2 /* a count was negative or above max_blocks */
+#define VGGT_STATUS_TIMEOUT 4   /* a bounded pipeline wait expired; output is invalid */
+#define VGGT_STATUS_BAD_HEAD 8  /* a head id was outside [0, heads); its rows were skipped */
+
+/* Library version, (major << 16) | minor. */
+int vggt_sparse_version(void);
+
+/* Message of the last argument error on the calling thread ("" if none). */
+const char* vggt_sparse_last_error(void);
+
+/*
+ * Block-sparse attention forward (with optional same-pass evidence).
+ * Replaces saf3r/triton/adaptive_block_attention.py:63-83 (block_attention)
+ * and its Triton kernel _forward (:7-60).
+ *
+ * head_dense  [n_slots] uint8 or NULL.  A slot whose flag is 1 attends to all
+ *             patch blocks in order (no index reads) plus the specials: the
+ *             dense path of the same kernel (head-profile dispatch).
+ * counts_per_qblock  0: counts is [n_slots]; 1: counts is [n_slots, n_qblocks].
+ * evidence    [n_slots, n_qblocks, max_blocks] fp32 or NULL.  When non-NULL,
+ *             slot j of a query block receives the mean, over valid query
+ *             rows, of the row log-sum-exp of that key block's logits
+ *             (adaptive_block_attention.py:29-33).  Slots >= count are not
+ *             written (callers pre-fill -inf).
+ * out         [heads, n_tokens, dim], same dtype as q.  Only rows of the
+ *             heads named in head_ids are written.
+ * kernel      VGGT_ATTN_*.
+ */
+int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v,
+                         const void* special_k, const void* special_v, int dtype,
+                         int64_t heads, int64_t n_tokens, int64_t n_patch, int64_t n_special,
+                         int dim, const int32_t* indices, const int32_t* counts,
+                         int counts_per_qblock, const int32_t* head_ids,
+                         const uint8_t* head_dense, int64_t n_slots, int64_t max_blocks,
+                         int block_q, int block_k, float scale, void* out, float* evidence,
+                         int32_t* status, int kernel, void* stream);
+
+/*
+ * Block-mask estimator.  Mean-pools q over query blocks of block_q tokens and
+ * patch_k over key blocks of block_k tokens (saf3r/patch/adaptive_block_value.py:16-23,
+ * applied to both), forms pooled scores S = (Qbar . Kbar^T) * scale in fp32
+ * (saf3r/patch/coarse_sensing.py:25-31), and selects key blocks per query
+ * block: top-k (adaptive_block_value.py:54-56, ties -> lower id) or the
+ * cumulative softmax-mass threshold tau (region_history_attention.py:39-42).
+ * Special tokens are never pooled: the attention kernel always attends them.
+ *
+ * head_ids       [n_slots] int32: heads to estimate (the sparse heads).
+ * pooled_q       caller scratch, fp32 [n_slots, ceil(n_tokens/block_q), dim]
+ * pooled_k       caller scratch, fp32 [n_slots, ceil(n_patch/block_k), dim]
+ * indices        out, int32 [n_slots, n_qblocks, max_blocks], ascending ids, -1 padded
+ * counts         out, int32 [n_slots, n_qblocks]
+ * scores         out or NULL, fp32 [n_slots, n_qblocks, n_blocks] pooled scores
+ * topk           VGGT_SELECT_TOPK: blocks kept per row (clamped to n_blocks)
+ * tau            VGGT_SELECT_MASS: mass threshold in (0, 1]
+ * max_blocks     >= min(topk, n_blocks) for top-k; >= n_blocks for mass
+ * status         device int32 or NULL; VGGT_STATUS_BAD_HEAD is ORed in for a
+ *                head id outside [0, heads) (its pooled rows are zero)
+ */
+int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int64_t heads,
+                             int64_t n_tokens, int64_t n_patch, int dim,
+                             const int32_t* head_ids, int64_t n_slots, int block_q,
+                             int block_k, int mode, int64_t topk, double tau, float scale,
+                             float* pooled_q, float* pooled_k, int32_t* indices,
+                             int64_t max_blocks, int32_t* counts, float* scores,
+                             int32_t* status, void* stream);
+
+/*
+ * Selection only, from caller-supplied fp32 pooled scores [rows, n_blocks]
+ * (row-major).  Used to re-run the selection rule on exported scores.
+ */
+int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int mode,
+                      int64_t topk, double tau, int32_t* indices, int64_t max_blocks,
+                      int32_t* counts, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VGGT_SPARSE_H */

@@ -1,0 +1,195 @@
+// extern "C" entry points: argument validation and dispatch.
+//
+// Error behaviour mirrors the reference operator, which raises ValueError
+// for unsupported dtypes (saf3r/triton/adaptive_block_attention.py:72-73):
+// here every argument error returns a negative code and leaves a message in
+// vggt_sparse_last_error(); nothing is launched in that case.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return -1;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int cuda_rc(cudaError_t e) {
+  if (e == cudaSuccess) return 0;
+  snprintf(g_err, sizeof(g_err), "CUDA error %d: %s", (int)e, cudaGetErrorString(e));
+  return (int)e;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+extern "C" {
+
+int vggt_sparse_version(void) { return (1 << 16) | 0; }
+
+const char* vggt_sparse_last_error(void) { return g_err; }
+
+int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v,
+                         const void* special_k, const void* special_v, int dtype, int64_t heads,
+                         int64_t n_tokens, int64_t n_patch, int64_t n_special, int dim,
+                         const int32_t* indices, const int32_t* counts, int counts_per_qblock,
+                         const int32_t* head_ids, const uint8_t* head_dense, int64_t n_slots,
+                         int64_t max_blocks, int block_q, int block_k, float scale, void* out,
+                         float* evidence, int32_t* status, int kernel, void* stream) {
+  g_err[0] = '\0';
+  if (dtype != VGGT_DTYPE_BF16 && dtype != VGGT_DTYPE_FP16)
+    return fail("Tensor-core sparse execution requires BF16 or FP16 (dtype code %d)", dtype);
+  if (dim != 32 && dim != 64) return fail("head dim %d unsupported (32 or 64)", dim);
+  if (block_q != 32 && block_q != 64) return fail("query_block %d unsupported (32, 64)", block_q);
+  if (block_k != 32 && block_k != 64 && block_k != 128)
+    return fail("key_block %d unsupported (32, 64, 128)", block_k);
+  if (heads < 1 || n_tokens < 0 || n_patch < 0 || n_special < 0 || n_slots < 0 || max_blocks < 0)
+    return fail("negative or empty size argument");
+  if (n_slots > 65535) return fail("n_slots %lld exceeds 65535", (long long)n_slots);
+  if (n_patch + n_special < 1 && n_tokens > 0 && n_slots > 0)
+    return fail("no keys: n_patch + n_special must be >= 1");
+  if (!std::isfinite(scale)) return fail("scale must be finite");
+  if (kernel != VGGT_ATTN_AUTO && kernel != VGGT_ATTN_MMA_SYNC && kernel != VGGT_ATTN_TCGEN05)
+    return fail("unknown kernel selector %d", kernel);
+  if (n_slots == 0 || n_tokens == 0) return 0;
+  if (!q || !patch_k || !patch_v || !out || !head_ids)
+    return fail("q, patch_k, patch_v, out and head_ids must be non-NULL");
+  if (n_special > 0 && (!special_k || !special_v))
+    return fail("special_k/special_v must be non-NULL when n_special > 0");
+  if (!counts || (max_blocks > 0 && !indices))
+    return fail("indices and counts must be non-NULL");
+  if (!aligned16(q) || !aligned16(patch_k) || !aligned16(patch_v) || !aligned16(out) ||
+      (n_special > 0 && (!aligned16(special_k) || !aligned16(special_v))))
+    return fail("q/k/v/out must be 16-byte aligned");
+
+  vggt::AttnArgs a;
+  a.q = q;
+  a.pk = patch_k;
+  a.pv = patch_v;
+  a.sk = special_k ? special_k : patch_k;
+  a.sv = special_v ? special_v : patch_v;
+  a.out = out;
+  a.indices = indices;
+  a.counts = counts;
+  a.head_ids = head_ids;
+  a.head_dense = head_dense;
+  a.evidence = evidence;
+  a.status = status;
+  a.heads = heads;
+  a.n_tokens = n_tokens;
+  a.n_patch = n_patch;
+  a.n_special = n_special;
+  a.n_slots = n_slots;
+  a.max_blocks = max_blocks;
+  a.qb_count = cdiv(n_tokens, block_q);
+  a.nb = cdiv(n_patch, block_k);
+  a.dim = dim;
+  a.block_q = block_q;
+  a.block_k = block_k;
+  a.dtype = dtype;
+  a.counts_per_qblock = counts_per_qblock ? 1 : 0;
+  a.scale = scale;
+  if (a.qb_count > 0x7fffffffLL) return fail("too many query blocks");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool tc_ok = vggt::attn_tc05_supported(a);
+  if (kernel == VGGT_ATTN_TCGEN05 && !tc_ok)
+    return fail("tcgen05 kernel does not support this shape (needs dim 64, block_q 64, block_k 64)");
+  if (kernel == VGGT_ATTN_TCGEN05 || (kernel == VGGT_ATTN_AUTO && tc_ok))
+    return cuda_rc(vggt::launch_attn_tc05(a, s));
+  return cuda_rc(vggt::launch_attn_mma(a, s));
+}
+
+int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int64_t heads,
+                             int64_t n_tokens, int64_t n_patch, int dim, const int32_t* head_ids,
+                             int64_t n_slots, int block_q, int block_k, int mode, int64_t topk,
+                             double tau, float scale, float* pooled_q, float* pooled_k,
+                             int32_t* indices, int64_t max_blocks, int32_t* counts, float* scores,
+                             int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (dtype != VGGT_DTYPE_BF16 && dtype != VGGT_DTYPE_FP16)
+    return fail("estimator requires BF16 or FP16 inputs (dtype code %d)", dtype);
+  if (dim != 32 && dim != 64) return fail("head dim %d unsupported (32 or 64)", dim);
+  if (block_q != 32 && block_q != 64 && block_q != 128)
+    return fail("query_block %d unsupported (32, 64, 128)", block_q);
+  if (block_k != 32 && block_k != 64 && block_k != 128)
+    return fail("key_block %d unsupported (32, 64, 128)", block_k);
+  if (heads < 1 || n_tokens < 0 || n_patch < 1 || n_slots < 0)
+    return fail("invalid sizes (need heads >= 1, n_patch >= 1)");
+  if (n_slots > 65535) return fail("n_slots %lld exceeds 65535", (long long)n_slots);
+  if (!std::isfinite(scale)) return fail("scale must be finite");
+  const int64_t qbc = cdiv(n_tokens, block_q), nb = cdiv(n_patch, block_k);
+  if (nb > vggt::estimator_max_blocks_supported(dim))
+    return fail("%lld key blocks exceed the supported maximum %d", (long long)nb,
+                vggt::estimator_max_blocks_supported(dim));
+  uint64_t tau_num = 0;
+  if (mode == VGGT_SELECT_TOPK) {
+    if (topk < 1) return fail("topk must be >= 1");
+    if (max_blocks < std::min<int64_t>(topk, nb))
+      return fail("max_blocks %lld < min(topk, n_blocks) = %lld", (long long)max_blocks,
+                  (long long)std::min<int64_t>(topk, nb));
+  } else if (mode == VGGT_SELECT_MASS) {
+    if (!(tau > 0.0 && tau <= 1.0)) return fail("tau must be in (0, 1]");
+    if (max_blocks < nb)
+      return fail("max_blocks %lld < n_blocks %lld (mass selection may keep every block)",
+                  (long long)max_blocks, (long long)nb);
+    tau_num = (uint64_t)std::floor(tau * (double)(1ull << vggt::kTauBits) + 0.5);
+    if (tau_num == 0) tau_num = 1;
+  } else {
+    return fail("unknown selection mode %d", mode);
+  }
+  if (n_slots == 0 || n_tokens == 0) return 0;
+  if (!q || !patch_k || !head_ids || !pooled_q || !pooled_k || !indices || !counts)
+    return fail("q, patch_k, head_ids, pooled_q, pooled_k, indices, counts must be non-NULL");
+  if (!aligned16(q) || !aligned16(patch_k) || !aligned16(pooled_q) || !aligned16(pooled_k))
+    return fail("q, patch_k and pooled scratch must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = cuda_rc(vggt::launch_pool(q, dtype, n_tokens, dim, block_q, qbc, head_ids, n_slots,
+                                     heads, pooled_q, status, s));
+  if (rc) return rc;
+  rc = cuda_rc(vggt::launch_pool(patch_k, dtype, n_patch, dim, block_k, nb, head_ids, n_slots,
+                                 heads, pooled_k, status, s));
+  if (rc) return rc;
+  return cuda_rc(vggt::launch_score_select(pooled_q, pooled_k, dim, qbc, nb, n_slots, scale, mode,
+                                           topk, tau_num, indices, max_blocks, counts, scores, s));
+}
+
+int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int mode, int64_t topk,
+                      double tau, int32_t* indices, int64_t max_blocks, int32_t* counts,
+                      void* stream) {
+  g_err[0] = '\0';
+  if (rows < 0 || n_blocks < 1) return fail("invalid sizes (need n_blocks >= 1)");
+  if (n_blocks > vggt::estimator_max_blocks_supported(0))
+    return fail("%lld blocks exceed the supported maximum", (long long)n_blocks);
+  uint64_t tau_num = 0;
+  if (mode == VGGT_SELECT_TOPK) {
+    if (topk < 1) return fail("topk must be >= 1");
+    if (max_blocks < std::min<int64_t>(topk, n_blocks)) return fail("max_blocks too small");
+  } else if (mode == VGGT_SELECT_MASS) {
+    if (!(tau > 0.0 && tau <= 1.0)) return fail("tau must be in (0, 1]");
+    if (max_blocks < n_blocks) return fail("max_blocks too small");
+    tau_num = (uint64_t)std::floor(tau * (double)(1ull << vggt::kTauBits) + 0.5);
+    if (tau_num == 0) tau_num = 1;
+  } else {
+    return fail("unknown selection mode %d", mode);
+  }
+  if (rows == 0) return 0;
+  if (!scores || !indices || !counts) return fail("scores, indices, counts must be non-NULL");
+  return cuda_rc(vggt::launch_select_from_scores(scores, rows, n_blocks, mode, topk, tau_num,
+                                                 indices, max_blocks, counts,
+                                                 static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,390 @@
+// Block-mask estimator: mean pooling of Q / patch-K per block, fp32 pooled
+// scores, and per-row selection (top-k or cumulative softmax mass).
+//
+// Reference behaviour restated here:
+//   pooling    saf3r/patch/adaptive_block_value.py:16-23 (block_mean; the last
+//              block divides by its real population)
+//   scores     saf3r/patch/coarse_sensing.py:25-31 (fp32 Q . Kbar^T * scale)
+//   top-k      saf3r/patch/adaptive_block_value.py:54-56 (topk, ids sorted);
+//              ties broken toward the lower block id as in
+//              saf3r/triton/fused_qk_topk.py:73-80
+//   mass       saf3r/patch/region_history_attention.py:39-42 (sort descending,
+//              cumsum, m = #(cumsum < tau) + 1, clamped to the row length)
+//
+// Both selection rules are one radix select over the monotone uint32 key of
+// the fp32 score: each of four 8-bit passes histograms (count, weight) of the
+// candidates sharing the decided prefix and keeps the highest digit whose
+// suffix weight still reaches the target.  Top-k uses unit weights and target
+// k; mass uses integer-quantised softmax weights (common.cuh) and target
+// ceil(tau * W).  Sums are exact integers, so the result does not depend on
+// summation order and the numpy oracle reproduces it bit for bit.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vggt {
+
+// ---------------------------------------------------------------------------
+// Pooling: one warp per (slot, block).  16-byte vector loads; each lane keeps
+// 8 fp32 column sums over the rows of its row group, then the row groups are
+// folded with shuffles in a fixed order.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256) pool_blocks_kernel(const T* __restrict__ x, int64_t len,
+                                                          int block, int64_t nblocks,
+                                                          const int32_t* __restrict__ head_ids,
+                                                          int64_t n_slots, int64_t heads,
+                                                          float* __restrict__ pooled,
+                                                          int32_t* __restrict__ status) {
+  constexpr int CH = D / 8;       // 16-byte chunks per row
+  constexpr int RG = 32 / CH;     // row groups per warp
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (unit >= n_slots * nblocks) return;
+  const int64_t slot = unit / nblocks;
+  const int64_t blk = unit - slot * nblocks;
+  const int64_t head = head_ids[slot];
+  const int chunk = lane % CH;
+  if (head < 0 || head >= heads) {
+    if (lane == 0 && status) atomicOr(status, VGGT_STATUS_BAD_HEAD);
+    if (lane < CH) {
+      float4* dst = reinterpret_cast<float4*>(pooled + unit * D + lane * 8);
+      dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return;
+  }
+  const int rg = lane / CH;
+  const int64_t row0 = blk * block;
+  const int64_t rows = min((int64_t)block, len - row0);
+  const uint4* src = reinterpret_cast<const uint4*>(x + (head * len + row0) * D) + chunk;
+
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  // up to 128 rows per block -> at most 32 iterations per lane
+#pragma unroll 4
+  for (int r = rg; r < rows; r += RG) {
+    uint4 v = __ldg(src + (int64_t)r * CH);
+    float2 a = ElemOps<T>::to_float2(v.x);
+    float2 b = ElemOps<T>::to_float2(v.y);
+    float2 c = ElemOps<T>::to_float2(v.z);
+    float2 d = ElemOps<T>::to_float2(v.w);
+    acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+    acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+  }
+#pragma unroll
+  for (int off = CH; off < 32; off <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
+  }
+  if (rg == 0) {
+    const float pop = (float)rows;
+    float4* dst = reinterpret_cast<float4*>(pooled + unit * D + chunk * 8);
+    dst[0] = make_float4(acc[0] / pop, acc[1] / pop, acc[2] / pop, acc[3] / pop);
+    dst[1] = make_float4(acc[4] / pop, acc[5] / pop, acc[6] / pop, acc[7] / pop);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Radix select of one row by one warp.
+// ---------------------------------------------------------------------------
+struct SelectHist {
+  unsigned long long w[256];
+  unsigned int c[256];
+};
+
+__device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
+  return (key & 0x80000000u) ? (key & 0x7fffffffu) : ~key;
+}
+
+// Writes ascending selected ids (and -1 padding) to out[0:max_blocks]; returns m.
+__device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode, int64_t topk,
+                               uint64_t tau_num, SelectHist* hist, int32_t* __restrict__ out,
+                               int64_t max_blocks) {
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  float rowmax = -INFINITY;
+  uint64_t target, total;
+  if (mode == VGGT_SELECT_MASS) {
+    for (int i = lane; i < nb; i += 32) rowmax = fmaxf(rowmax, srow[i]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) rowmax = fmaxf(rowmax, __shfl_xor_sync(full, rowmax, off));
+    unsigned long long tw = 0;
+    for (int i = lane; i < nb; i += 32) tw += det_mass_weight(srow[i], rowmax);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) tw += __shfl_xor_sync(full, tw, off);
+    total = tw;
+    target = mass_target(total, tau_num);
+  } else {
+    total = (uint64_t)nb;
+    target = (uint64_t)(topk < (int64_t)nb ? topk : (int64_t)nb);
+  }
+
+  int m;
+  // Every block is kept when k >= nb, or when no prefix reaches the mass target
+  // (m = #(cum < T) + 1 then exceeds nb and is clamped).  A mass target equal to
+  // the total still goes through the radix path: trailing zero-weight blocks
+  // are excluded exactly as the reference's cumsum would exclude them.
+  if (target > total || (mode == VGGT_SELECT_TOPK && target == total)) {
+    m = nb;
+    for (int i = lane; i < nb; i += 32)
+      if (i < max_blocks) out[i] = i;
+  } else {
+    uint32_t prefix = 0, prefix_mask = 0;
+    unsigned long long above_w = 0;
+    unsigned int above_c = 0;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = lane; b < 256; b += 32) {
+        hist->w[b] = 0ull;
+        hist->c[b] = 0u;
+      }
+      __syncwarp();
+      for (int i = lane; i < nb; i += 32) {
+        const float s = srow[i];
+        const uint32_t key = score_key(s);
+        if ((key & prefix_mask) == prefix) {
+          const int dgt = (key >> shift) & 255;
+          const unsigned long long w =
+              (mode == VGGT_SELECT_MASS) ? (unsigned long long)det_mass_weight(s, rowmax) : 1ull;
+          atomicAdd(&hist->w[dgt], w);
+          atomicAdd(&hist->c[dgt], 1u);
+        }
+      }
+      __syncwarp();
+      // lane L owns digits 8L .. 8L+7
+      unsigned long long lw[8];
+      unsigned int lc[8];
+      unsigned long long lane_w = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        lw[j] = hist->w[8 * lane + j];
+        lc[j] = hist->c[8 * lane + j];
+        lane_w += lw[j];
+      }
+      // exclusive suffix sum over higher lanes
+      unsigned long long suffix = lane_w;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        unsigned long long v = __shfl_down_sync(full, suffix, off);
+        if (lane + off < 32) suffix += v;
+      }
+      unsigned long long above_lane = suffix - lane_w;  // digits of higher lanes
+      int found = -1;
+      unsigned long long run = above_w + above_lane;
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {
+        if (found < 0) {
+          if (run + lw[j] >= target) found = j;
+          else run += lw[j];
+        }
+      }
+      const unsigned ball = __ballot_sync(full, found >= 0);
+      const int win = 31 - __clz(ball);  // highest lane holding a qualifying digit
+      // winner: run = above_w + weight of digits strictly above the found one
+      unsigned long long new_above_w = run;
+      unsigned int cnt_above = 0;
+      if (lane == win) {
+        // count of digits strictly above `found` inside this lane
+        for (int j = 7; j > found; --j) cnt_above += lc[j];
+      }
+      // counts of higher lanes
+      unsigned int lane_c = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) lane_c += lc[j];
+      unsigned int csuffix = lane_c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        unsigned int v = __shfl_down_sync(full, csuffix, off);
+        if (lane + off < 32) csuffix += v;
+      }
+      cnt_above += csuffix - lane_c;
+      const int digit = __shfl_sync(full, 8 * lane + found, win);
+      above_w = __shfl_sync(full, new_above_w, win);
+      above_c += __shfl_sync(full, cnt_above, win);
+      prefix |= (uint32_t)digit << shift;
+      prefix_mask |= 255u << shift;
+      __syncwarp();
+    }
+    // prefix is now the key of the last selected element
+    unsigned long long tie_w = 1ull;
+    if (mode == VGGT_SELECT_MASS) tie_w = det_mass_weight(__uint_as_float(key_to_bits(prefix)), rowmax);
+    const unsigned long long need = target - above_w;  // > 0
+    const unsigned int ties_taken = (unsigned int)((need + tie_w - 1ull) / tie_w);
+    m = (int)(above_c + ties_taken);
+    // compaction in id order
+    unsigned int tie_seen = 0, written = 0;
+    for (int base = 0; base < nb; base += 32) {
+      const int i = base + lane;
+      uint32_t key = 0;
+      bool valid = i < nb;
+      if (valid) key = score_key(srow[i]);
+      const bool gt = valid && key > prefix;
+      const bool eq = valid && key == prefix;
+      const unsigned eqb = __ballot_sync(full, eq);
+      const unsigned rank = tie_seen + __popc(eqb & lt_mask);
+      const bool inc = gt || (eq && rank < ties_taken);
+      const unsigned incb = __ballot_sync(full, inc);
+      const unsigned pos = written + __popc(incb & lt_mask);
+      if (inc && pos < max_blocks) out[pos] = i;
+      written += __popc(incb);
+      tie_seen += __popc(eqb);
+    }
+  }
+  for (int64_t j = m + lane; j < max_blocks; j += 32) out[j] = -1;
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// Scores + selection.  One CTA holds R query blocks of one slot: their pooled
+// Q rows and their complete fp32 score rows live in shared memory; pooled K
+// is streamed once per CTA.  Warps then select rows independently.
+// ---------------------------------------------------------------------------
+template <int D, bool FROM_SCORES>
+__global__ void __launch_bounds__(256) score_select_kernel(
+    const float* __restrict__ pooled_q, const float* __restrict__ pooled_k, int64_t qb_count,
+    int64_t nb, int rows_per_cta, float scale, int mode, int64_t topk, uint64_t tau_num,
+    int32_t* __restrict__ indices, int64_t max_blocks, int32_t* __restrict__ counts,
+    float* __restrict__ scores_out, const float* __restrict__ scores_in) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SelectHist* hist = reinterpret_cast<SelectHist*>(smem_raw);  // [8]
+  float* qbar = reinterpret_cast<float*>(hist + 8);           // [R][D]
+  float* srows = qbar + (FROM_SCORES ? 0 : rows_per_cta * D); // [R][nb]
+
+  const int64_t slot = blockIdx.y;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int rows = (int)(qb_count - r0 < rows_per_cta ? qb_count - r0 : rows_per_cta);
+  const int tid = threadIdx.x;
+
+  if constexpr (FROM_SCORES) {
+    // rows are [slot*qb_count + r] of a [rows, nb] matrix
+    for (int r = 0; r < rows; ++r) {
+      const float* src = scores_in + (slot * qb_count + r0 + r) * nb;
+      for (int64_t i = tid; i < nb; i += blockDim.x) srows[r * nb + i] = src[i];
+    }
+  } else {
+    const float* qsrc = pooled_q + (slot * qb_count + r0) * D;
+    for (int i = tid; i < rows * D; i += blockDim.x) qbar[i] = qsrc[i];
+    __syncthreads();
+    const float* ksrc = pooled_k + slot * nb * D;
+    for (int64_t kb = tid; kb < nb; kb += blockDim.x) {
+      float kv[D];
+      const float4* kp = reinterpret_cast<const float4*>(ksrc + kb * D);
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) {
+        float4 t = __ldg(kp + i);
+        kv[4 * i] = t.x; kv[4 * i + 1] = t.y; kv[4 * i + 2] = t.z; kv[4 * i + 3] = t.w;
+      }
+      for (int r = 0; r < rows; ++r) {
+        const float* qr = qbar + r * D;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) acc = fmaf(qr[i], kv[i], acc);
+        const float s = acc * scale;
+        srows[r * nb + kb] = s;
+        if (scores_out) scores_out[(slot * qb_count + r0 + r) * nb + kb] = s;
+      }
+    }
+  }
+  __syncthreads();
+  const int warp = tid >> 5;
+  for (int r = warp; r < rows; r += (blockDim.x >> 5)) {
+    const int64_t row = slot * qb_count + r0 + r;
+    int m = select_row_warp(srows + (int64_t)r * nb, (int)nb, mode, topk, tau_num, hist + warp,
+                            indices + row * max_blocks, max_blocks);
+    if ((threadIdx.x & 31) == 0) counts[row] = m;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+static int select_rows_per_cta(int64_t nb, int d, int64_t qb_count, bool from_scores) {
+  const int64_t budget = 200 * 1024 - 8 * (int64_t)sizeof(SelectHist);
+  const int64_t per_row = nb * 4 + (from_scores ? 0 : d * 4);
+  int64_t r = budget / per_row;
+  r = std::min<int64_t>(r, 32);
+  r = std::min<int64_t>(r, qb_count);
+  return (int)r;
+}
+
+static size_t select_smem_bytes(int rows, int64_t nb, int d, bool from_scores) {
+  return 8 * sizeof(SelectHist) + (size_t)rows * ((from_scores ? 0 : d) + nb) * 4;
+}
+
+template <int D, bool FROM>
+static cudaError_t launch_select_t(const float* pq, const float* pk, int64_t qb_count, int64_t nb,
+                                   int64_t n_slots, float scale, int mode, int64_t topk,
+                                   uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                   int32_t* counts, float* scores_out, const float* scores_in,
+                                   cudaStream_t stream) {
+  const int rows = select_rows_per_cta(nb, D, qb_count, FROM);
+  if (rows < 1) return cudaErrorInvalidValue;
+  const size_t smem = select_smem_bytes(rows, nb, D, FROM);
+  auto kern = score_select_kernel<D, FROM>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((qb_count + rows - 1) / rows), (unsigned)n_slots);
+  kern<<<grid, 256, smem, stream>>>(pq, pk, qb_count, nb, rows, scale, mode, topk, tau_num,
+                                     indices, max_blocks, counts, scores_out, scores_in);
+  return cudaGetLastError();
+}
+
+int estimator_max_blocks_supported(int d) {
+  // largest nb with at least one row per CTA
+  const int64_t budget = 200 * 1024 - 8 * (int64_t)sizeof(SelectHist);
+  return (int)(budget / 4 - d);
+}
+
+template <typename T>
+static cudaError_t launch_pool_t(const void* x, int64_t len, int d, int block, int64_t nblocks,
+                                 const int32_t* head_ids, int64_t n_slots, int64_t heads,
+                                 float* pooled, int32_t* status, cudaStream_t stream) {
+  const int64_t units = n_slots * nblocks;
+  const int warps = 8;
+  dim3 grid((unsigned)((units + warps - 1) / warps));
+  if (d == 64)
+    pool_blocks_kernel<T, 64><<<grid, warps * 32, 0, stream>>>(
+        static_cast<const T*>(x), len, block, nblocks, head_ids, n_slots, heads, pooled, status);
+  else
+    pool_blocks_kernel<T, 32><<<grid, warps * 32, 0, stream>>>(
+        static_cast<const T*>(x), len, block, nblocks, head_ids, n_slots, heads, pooled, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool(const void* x, int dtype, int64_t len, int d, int block, int64_t nblocks,
+                        const int32_t* head_ids, int64_t n_slots, int64_t heads, float* pooled,
+                        int32_t* status, cudaStream_t stream) {
+  if (units_zero(n_slots, nblocks)) return cudaSuccess;
+  if (dtype == VGGT_DTYPE_BF16)
+    return launch_pool_t<__nv_bfloat16>(x, len, d, block, nblocks, head_ids, n_slots, heads,
+                                        pooled, status, stream);
+  return launch_pool_t<__half>(x, len, d, block, nblocks, head_ids, n_slots, heads, pooled,
+                               status, stream);
+}
+
+cudaError_t launch_score_select(const float* pq, const float* pk, int d, int64_t qb_count,
+                                int64_t nb, int64_t n_slots, float scale, int mode, int64_t topk,
+                                uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                int32_t* counts, float* scores_out, cudaStream_t stream) {
+  if (units_zero(n_slots, qb_count)) return cudaSuccess;
+  if (d == 64)
+    return launch_select_t<64, false>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                      indices, max_blocks, counts, scores_out, nullptr, stream);
+  return launch_select_t<32, false>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                    indices, max_blocks, counts, scores_out, nullptr, stream);
+}
+
+cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int64_t nb, int mode,
+                                      int64_t topk, uint64_t tau_num, int32_t* indices,
+                                      int64_t max_blocks, int32_t* counts, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  return launch_select_t<32, true>(nullptr, nullptr, rows, nb, 1, 1.f, mode, topk, tau_num,
+                                   indices, max_blocks, counts, nullptr, scores, stream);
+}
+
+}  // namespace vggt

@@ -1,0 +1,50 @@
+// Internal launcher declarations shared by the C-ABI translation unit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vggt {
+
+inline bool units_zero(int64_t a, int64_t b) { return a == 0 || b == 0; }
+
+// estimator.cu
+cudaError_t launch_pool(const void* x, int dtype, int64_t len, int d, int block, int64_t nblocks,
+                        const int32_t* head_ids, int64_t n_slots, int64_t heads, float* pooled,
+                        int32_t* status, cudaStream_t stream);
+cudaError_t launch_score_select(const float* pq, const float* pk, int d, int64_t qb_count,
+                                int64_t nb, int64_t n_slots, float scale, int mode, int64_t topk,
+                                uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                int32_t* counts, float* scores_out, cudaStream_t stream);
+cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int64_t nb, int mode,
+                                      int64_t topk, uint64_t tau_num, int32_t* indices,
+                                      int64_t max_blocks, int32_t* counts, cudaStream_t stream);
+int estimator_max_blocks_supported(int d);
+
+// Arguments of one block-sparse attention launch (device pointers).
+struct AttnArgs {
+  const void* q;
+  const void* pk;
+  const void* pv;
+  const void* sk;
+  const void* sv;
+  void* out;
+  const int32_t* indices;
+  const int32_t* counts;
+  const int32_t* head_ids;
+  const uint8_t* head_dense;
+  float* evidence;
+  int32_t* status;
+  int64_t heads, n_tokens, n_patch, n_special;
+  int64_t n_slots, max_blocks, qb_count, nb;
+  int dim, block_q, block_k, dtype, counts_per_qblock;
+  float scale;
+};
+
+// attn_mma.cu
+cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
+// attn_tc05.cu
+bool attn_tc05_supported(const AttnArgs& a);
+cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream);
+
+}  // namespace vggt

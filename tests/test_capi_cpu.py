@@ -1,0 +1,128 @@
+"""C-ABI library: loads, exports every declared symbol, validates arguments.
+No kernel is launched (argument errors return before any CUDA call)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "vggt_sparse.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(vggt_\w+)\s*\(", text, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from vggt_sparse import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        from vggt_sparse.build import build
+        build()
+    return _lib.load()
+
+
+def test_header_declares_the_documented_entry_points():
+    assert declared_symbols() == sorted([
+        "vggt_block_attention", "vggt_block_mask_estimate", "vggt_block_select",
+        "vggt_sparse_last_error", "vggt_sparse_version"])
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from vggt_sparse import _lib
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, name
+
+
+def test_version(lib):
+    assert lib.vggt_sparse_version() == (1 << 16)
+
+
+def _attn(lib, **kw):
+    args = dict(q=16, pk=16, pv=16, sk=16, sv=16, dtype=0, heads=2, n=128, npatch=64, nspecial=5,
+                dim=64, indices=16, counts=16, per_row=0, head_ids=16, dense=None, slots=1,
+                maxk=1, bq=64, bk=64, scale=0.125, out=16, ev=None, status=None, kernel=0,
+                stream=None)
+    args.update(kw)
+    return lib.vggt_block_attention(*args.values())
+
+
+@pytest.mark.parametrize("bad,msg", [
+    (dict(dtype=5), "BF16 or FP16"),
+    (dict(dim=128), "head dim"),
+    (dict(bq=16), "query_block"),
+    (dict(bk=256), "key_block"),
+    (dict(heads=0), "size"),
+    (dict(npatch=0, nspecial=0), "no keys"),
+    (dict(scale=float("inf")), "finite"),
+    (dict(kernel=9), "kernel"),
+    (dict(q=None), "non-NULL"),
+    (dict(q=8), "aligned"),
+    (dict(slots=70000), "65535"),
+])
+def test_attention_argument_errors(lib, bad, msg):
+    rc = _attn(lib, **bad)
+    assert rc < 0
+    assert msg in lib.vggt_sparse_last_error().decode()
+
+
+def test_attention_empty_is_a_no_op(lib):
+    assert _attn(lib, slots=0) == 0
+    assert _attn(lib, n=0) == 0
+
+
+def _est(lib, **kw):
+    args = dict(q=16, kp=16, dtype=0, heads=2, n=128, npatch=64, dim=64, head_ids=16, slots=1,
+                bq=64, bk=64, mode=0, topk=1, tau=0.0, scale=0.125, pq=16, pk=16, idx=16,
+                maxk=1, counts=16, scores=None, status=None, stream=None)
+    args.update(kw)
+    return lib.vggt_block_mask_estimate(*args.values())
+
+
+@pytest.mark.parametrize("bad,msg", [
+    (dict(dtype=2), "BF16 or FP16"),
+    (dict(mode=0, topk=0), "topk"),
+    (dict(mode=0, topk=4, maxk=0), "max_blocks"),
+    (dict(mode=1, tau=0.0, maxk=1), "tau"),
+    (dict(mode=1, tau=1.5, maxk=1), "tau"),
+    (dict(mode=1, tau=0.9, maxk=0), "max_blocks"),
+    (dict(mode=7), "mode"),
+    (dict(npatch=0), "n_patch"),
+    (dict(npatch=64 * 60000), "exceed"),
+    (dict(pq=None), "non-NULL"),
+])
+def test_estimator_argument_errors(lib, bad, msg):
+    rc = _est(lib, **bad)
+    assert rc < 0
+    assert msg in lib.vggt_sparse_last_error().decode()
+
+
+def test_select_argument_errors(lib):
+    assert lib.vggt_block_select(16, 4, 0, 0, 1, 0.0, 16, 1, 16, None) < 0
+    assert lib.vggt_block_select(16, 4, 10, 1, 0, 0.9, 16, 5, 16, None) < 0
+    assert lib.vggt_block_select(16, 0, 10, 0, 3, 0.0, 16, 3, 16, None) == 0
+
+
+def test_python_layer_rejects_cpu_tensors_and_fp32():
+    import torch
+    import vggt_sparse
+    q = torch.zeros(2, 8, 64, dtype=torch.float32)
+    with pytest.raises(ValueError, match="BF16 or FP16"):
+        vggt_sparse.block_attention(q, q, q, q, q, torch.zeros(1, 1, 1, dtype=torch.int32),
+                                    torch.zeros(1, dtype=torch.int32),
+                                    torch.zeros(1, dtype=torch.int32))
+    qb = q.to(torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        vggt_sparse.block_attention(qb, qb, qb, qb, qb, torch.zeros(1, 1, 1, dtype=torch.int32),
+                                    torch.zeros(1, dtype=torch.int32),
+                                    torch.zeros(1, dtype=torch.int32), validate=False)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    from vggt_sparse import _lib
+    with pytest.raises(_lib.ExtensionMissing):
+        _lib.load(str(tmp_path / "missing.so"))
