@@ -1,11 +1,524 @@
-// tcgen05 / TMEM / TMA block-sparse attention (work in progress).
+// Block-sparse attention forward on the 5th-generation tensor cores.
+//
+// Computes what saf3r/triton/adaptive_block_attention.py:7-60 computes (exact
+// softmax over each query block's selected 64-key patch blocks plus all
+// special keys, fp32 online softmax) with a different decomposition:
+//
+//  * one CTA = 128 query rows = two adjacent 64-row query blocks (2p, 2p+1)
+//    of one slot (head).  The key tiles are the ascending union of the two
+//    blocks' selections; a tile selected by only one block is masked to -inf
+//    for the other block's 64 rows, so every output row sees exactly its own
+//    key set.  This keeps tcgen05 at M=128, its full-rate shape.
+//  * warp 0 (one lane) streams K and V tiles with TMA (3-D tensor maps over
+//    [heads, rows, 64], 128-byte swizzle, zero fill past the end of a head)
+//    into a 4-stage ring; warp 1 (one lane) issues the MMAs
+//      S_t  = Q K_t^T  (SS, 128x64x64, fp32 in TMEM, double-buffered)
+//      PV_t = P_t V_t  (TS: P read from TMEM where it overwrote S_t)
+//    and warps 2-5 (128 threads, one query row each) run the softmax: read
+//    S_t, mask, exp2 with the running max, write P_t (bf16/fp16) back to TMEM,
+//    then fold PV_{t-1} into a register accumulator with the exact rescale
+//    factor exp2(m_old - m_new).
+//  * dense-profiled slots walk every patch block (no index reads): the dense
+//    path of the same kernel.
+//
+// Every mbarrier wait is bounded (1 s); on expiry the CTA raises an abort
+// flag, records VGGT_STATUS_TIMEOUT, drains its in-flight copies, frees its
+// TMEM and exits.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tc05.cuh"
 
 namespace vggt {
 
-bool attn_tc05_supported(const AttnArgs&) { return false; }
+namespace tcattn {
 
-cudaError_t launch_attn_tc05(const AttnArgs&, cudaStream_t) { return cudaErrorNotSupported; }
+constexpr int BM = 128;         // query rows per CTA
+constexpr int BN = 64;          // keys per tile
+constexpr int HD = 64;          // head dim
+constexpr int NSTAGE = 4;       // K/V ring depth
+constexpr int THREADS = 192;
+constexpr uint32_t TILE_BYTES = BN * HD * 2;  // 8 KB
+constexpr uint32_t Q_BYTES = BM * HD * 2;     // 16 KB
+constexpr uint32_t TMEM_COLS = 256;           // S0 | S1 | PV0 | PV1
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
+
+// shared-memory layout (offsets from a 1024-aligned base)
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+constexpr uint32_t OFF_V = OFF_K + NSTAGE * TILE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + NSTAGE * TILE_BYTES;
+// barrier indices
+constexpr int B_QFULL = 0;
+constexpr int B_KVFULL = 1;                 // [NSTAGE]
+constexpr int B_KVEMPTY = B_KVFULL + NSTAGE;  // [NSTAGE]
+constexpr int B_SFULL = B_KVEMPTY + NSTAGE;   // [2]
+constexpr int B_PFULL = B_SFULL + 2;          // [2]
+constexpr int B_PVFULL = B_PFULL + 2;         // [2]
+constexpr int B_PVEMPTY = B_PVFULL + 2;       // [2]
+constexpr int B_DRAIN = B_PVEMPTY + 2;        // MMA completion before TMEM release
+constexpr int NBAR = B_DRAIN + 1;
+constexpr uint32_t OFF_META = OFF_BAR + NBAR * 8;       // int[NSTAGE]
+constexpr uint32_t OFF_MISC = OFF_META + NSTAGE * 4;    // tmem base, abort, tiles, scratch
+constexpr uint32_t OFF_BITMAP = (OFF_MISC + 64 + 15) & ~15u;
+
+struct Params {
+  const int32_t* indices;
+  const int32_t* counts;
+  const int32_t* head_ids;
+  const uint8_t* head_dense;
+  void* out;
+  int32_t* status;
+  int64_t heads, n_tokens, n_patch, n_special, n_slots, max_blocks, qb_count, nb, pairs;
+  int counts_per_qblock;
+  float scale_log2;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 2)
+    attn_tc05_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_kp,
+                     const __grid_constant__ CUtensorMap tm_vp,
+                     const __grid_constant__ CUtensorMap tm_ks,
+                     const __grid_constant__ CUtensorMap tm_vs, Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  unsigned char* sbase = smem_raw + (base - raw_addr);
+  const uint32_t bar0 = base + OFF_BAR;
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  volatile int* meta = reinterpret_cast<volatile int*>(sbase + OFF_META);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
+  uint32_t* bm = reinterpret_cast<uint32_t*>(sbase + OFF_BITMAP);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- work decode: dense-heavy slots (last in the slot order) go first ----
+  const int64_t w = blockIdx.x;
+  const int64_t slot = p.n_slots - 1 - w / p.pairs;
+  const int64_t pair = w % p.pairs;
+  const int64_t head = p.head_ids[slot];
+  if (head < 0 || head >= p.heads) {
+    if (tid == 0 && p.status) atomicOr(p.status, VGGT_STATUS_BAD_HEAD);
+    return;
+  }
+  const bool dense = p.head_dense != nullptr && p.head_dense[slot] != 0;
+  const int64_t qb0 = 2 * pair, qb1 = qb0 + 1;
+  const bool has1 = qb1 < p.qb_count;
+  const int nwords = (int)((p.nb + 31) >> 5);
+  uint32_t* bmA = bm;
+  uint32_t* bmB = bm + nwords;
+
+  // ---- union of the two query blocks' selections as two bitmaps ----
+  int64_t n_patch_tiles;
+  if (dense) {
+    n_patch_tiles = p.nb;
+  } else {
+    int64_t c0 = p.counts_per_qblock ? p.counts[slot * p.qb_count + qb0] : p.counts[slot];
+    int64_t c1 = has1 ? (p.counts_per_qblock ? p.counts[slot * p.qb_count + qb1] : c0) : 0;
+    if (c0 < 0 || c0 > p.max_blocks || c1 < 0 || c1 > p.max_blocks) {
+      if (tid == 0 && p.status) atomicOr(p.status, VGGT_STATUS_BAD_COUNT);
+      c0 = c0 < 0 ? 0 : (c0 > p.max_blocks ? p.max_blocks : c0);
+      c1 = c1 < 0 ? 0 : (c1 > p.max_blocks ? p.max_blocks : c1);
+    }
+    for (int i = tid; i < 2 * nwords; i += THREADS) bm[i] = 0u;
+    if (tid == 0) misc[2] = 0u;
+    __syncthreads();
+    const int32_t* row0 = p.indices + (slot * p.qb_count + qb0) * p.max_blocks;
+    const int32_t* row1 = row0 + p.max_blocks;
+    bool bad = false;
+    for (int64_t i = tid; i < c0; i += THREADS) {
+      const int32_t kb = row0[i];
+      if (kb >= 0 && kb < p.nb) atomicOr(&bmA[kb >> 5], 1u << (kb & 31));
+      else bad = true;
+    }
+    for (int64_t i = tid; i < c1; i += THREADS) {
+      const int32_t kb = row1[i];
+      if (kb >= 0 && kb < p.nb) atomicOr(&bmB[kb >> 5], 1u << (kb & 31));
+      else bad = true;
+    }
+    if (bad && p.status) atomicOr(p.status, VGGT_STATUS_BAD_INDEX);
+    __syncthreads();
+    uint32_t cnt = 0;
+    for (int i = tid; i < nwords; i += THREADS) cnt += __popc(bmA[i] | bmB[i]);
+    for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+    if (lane == 0 && cnt) atomicAdd(&misc[2], cnt);
+    __syncthreads();
+    n_patch_tiles = misc[2];
+  }
+  const int64_t n_spec_tiles = (p.n_special + BN - 1) / BN;
+  const int64_t n_tiles = n_patch_tiles + n_spec_tiles;
+
+  // ---- barriers and TMEM ----
+  if (tid == 0) {
+    tc::mbar_init(bar(B_QFULL), 1);
+    for (int s = 0; s < NSTAGE; ++s) {
+      tc::mbar_init(bar(B_KVFULL + s), 1);
+      tc::mbar_init(bar(B_KVEMPTY + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(bar(B_SFULL + b), 1);
+      tc::mbar_init(bar(B_PFULL + b), 128);
+      tc::mbar_init(bar(B_PVFULL + b), 1);
+      tc::mbar_init(bar(B_PVEMPTY + b), 128);
+    }
+    tc::mbar_init(bar(B_DRAIN), 1);
+    misc[1] = 0u;  // abort flag
+    tc::mbar_fence_init();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(base + OFF_MISC, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = misc[0];
+  const uint32_t t_s[2] = {tmem + 0u, tmem + 64u};
+  const uint32_t t_pv[2] = {tmem + 128u, tmem + 192u};
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_q);
+      tc::prefetch_tmap(&tm_kp);
+      tc::prefetch_tmap(&tm_vp);
+      tc::mbar_expect_tx(bar(B_QFULL), Q_BYTES);
+      tc::tma_load_3d(base + OFF_Q, &tm_q, bar(B_QFULL), 0, (int)(qb0 * 64), (int)head);
+      int wi = 0;
+      uint32_t cur = 0, curA = 0;
+      if (!dense && nwords > 0) {
+        curA = bmA[0];
+        cur = curA | bmB[0];
+      }
+      int64_t issued = 0;
+      for (int64_t t = 0; t < n_tiles; ++t) {
+        const int stage = (int)(t % NSTAGE);
+        if (t >= NSTAGE) {
+          if (!tc::mbar_wait(bar(B_KVEMPTY + stage), (uint32_t)((t / NSTAGE - 1) & 1), abort_flag,
+                             WAIT_LIMIT_NS))
+            break;
+        }
+        int flags, ncols, row;
+        const CUtensorMap *mk, *mv;
+        if (t < n_patch_tiles) {
+          int64_t kb;
+          if (dense) {
+            kb = t;
+            flags = 3;
+          } else {
+            while (cur == 0u) {
+              ++wi;
+              curA = bmA[wi];
+              cur = curA | bmB[wi];
+            }
+            const int b = __ffs(cur) - 1;
+            cur &= cur - 1u;
+            kb = (int64_t)wi * 32 + b;
+            flags = (int)((curA >> b) & 1u) | (int)(((bmB[wi] >> b) & 1u) << 1);
+          }
+          row = (int)(kb * BN);
+          ncols = (int)(p.n_patch - kb * BN < BN ? p.n_patch - kb * BN : BN);
+          mk = &tm_kp;
+          mv = &tm_vp;
+        } else {
+          const int64_t st = t - n_patch_tiles;
+          flags = 3;
+          row = (int)(st * BN);
+          ncols = (int)(p.n_special - st * BN < BN ? p.n_special - st * BN : BN);
+          mk = &tm_ks;
+          mv = &tm_vs;
+        }
+        if (t == n_tiles - 1) flags |= 4;
+        meta[stage] = flags | (ncols << 8);
+        tc::mbar_expect_tx(bar(B_KVFULL + stage), 2 * TILE_BYTES);
+        tc::tma_load_3d(base + OFF_K + stage * TILE_BYTES, mk, bar(B_KVFULL + stage), 0, row,
+                        (int)head);
+        tc::tma_load_3d(base + OFF_V + stage * TILE_BYTES, mv, bar(B_KVFULL + stage), 0, row,
+                        (int)head);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // drain: wait (bounded) for every copy this thread issued
+        tc::mbar_wait_drain(bar(B_QFULL), 0, WAIT_LIMIT_NS);
+        const int64_t first = issued > NSTAGE ? issued - NSTAGE : 0;
+        for (int64_t t = first; t < issued; ++t)
+          tc::mbar_wait_drain(bar(B_KVFULL + (int)(t % NSTAGE)), (uint32_t)((t / NSTAGE) & 1),
+                              WAIT_LIMIT_NS);
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t id_qk = tc::idesc_f16(fmt, 0u, BM, BN);
+      const uint32_t id_pv = tc::idesc_f16(fmt, 1u, BM, HD);
+      const uint64_t qdesc = tc::sw128_desc(base + OFF_Q, 16);
+      bool ok = tc::mbar_wait(bar(B_QFULL), 0, abort_flag, WAIT_LIMIT_NS);
+      auto issue_pv = [&](int64_t u) -> bool {
+        const int bu = (int)(u & 1);
+        const int su = (int)(u % NSTAGE);
+        if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
+          return false;
+        if (u >= 2 && !tc::mbar_wait(bar(B_PVEMPTY + bu), (uint32_t)(((u >> 1) - 1) & 1),
+                                     abort_flag, WAIT_LIMIT_NS))
+          return false;
+        tc::tc_fence_after();
+        const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES, 8192);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc::mma_ts(t_pv[bu], t_s[bu] + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
+                     kk > 0 ? 1u : 0u);
+        tc::mma_commit(bar(B_PVFULL + bu));
+        tc::mma_commit(bar(B_KVEMPTY + su));
+        return true;
+      };
+      for (int64_t t = 0; ok && t < n_tiles; ++t) {
+        const int stage = (int)(t % NSTAGE);
+        const int b = (int)(t & 1);
+        if (!tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
+                           WAIT_LIMIT_NS)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint64_t kdesc = tc::sw128_desc(base + OFF_K + stage * TILE_BYTES, 16);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc::mma_ss(t_s[b], qdesc + (uint64_t)(kk * 2), kdesc + (uint64_t)(kk * 2), id_qk,
+                     kk > 0 ? 1u : 0u);
+        tc::mma_commit(bar(B_SFULL + b));
+        if (t >= 1 && !issue_pv(t - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+      // every issued MMA must finish before the TMEM columns are released
+      tc::mma_commit(bar(B_DRAIN));
+      tc::mbar_wait_drain(bar(B_DRAIN), 0, WAIT_LIMIT_NS);
+    }
+  } else {
+    // ================= softmax: warps 2..5, one query row per thread ============
+    const int sub = warp & 3;                 // TMEM lane quarter of this warp
+    const int row = sub * 32 + lane;          // 0..127
+    const int half = row >> 6;                // which query block of the pair
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    float o[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, m_acc = -INFINITY, m_prev = -INFINITY;
+    bool ok = true;
+
+    auto accumulate = [&](int64_t u, float m_u) -> bool {
+      const int bu = (int)(u & 1);
+      if (!tc::mbar_wait(bar(B_PVFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
+        return false;
+      tc::tc_fence_after();
+      uint32_t r[32];
+      const float f = (m_acc == m_u) ? 1.f : ex2(m_acc - m_u);
+      tc::tmem_ld32(t_pv[bu] + lane_off, r);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], f, __uint_as_float(r[i]));
+      tc::tmem_ld32(t_pv[bu] + lane_off + 32u, r);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[32 + i] = fmaf(o[32 + i], f, __uint_as_float(r[i]));
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar(B_PVEMPTY + bu));
+      m_acc = m_u;
+      return true;
+    };
+
+    for (int64_t t = 0; t < n_tiles; ++t) {
+      const int stage = (int)(t % NSTAGE);
+      const int b = (int)(t & 1);
+      if (!tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
+                         WAIT_LIMIT_NS) ||
+          !tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1), abort_flag, WAIT_LIMIT_NS)) {
+        ok = false;
+        break;
+      }
+      const int mt = meta[stage];
+      const int ncols = (mt >> 8) & 0xff;
+      const bool active = (mt >> half) & 1;
+      tc::tc_fence_after();
+      uint32_t s[64];
+      tc::tmem_ld32(t_s[b] + lane_off, s);
+      tc::tmem_ld32(t_s[b] + lane_off + 32u, s + 32);
+      tc::tmem_wait_ld();
+      uint32_t pk[32];
+      if (active) {
+        float mloc = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float x = (i < ncols) ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY;
+          s[i] = __float_as_uint(x);
+          mloc = fmaxf(mloc, x);
+        }
+        const float m_new = fmaxf(m, mloc);
+        const float corr = (m == m_new) ? 1.f : ex2(m - m_new);
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = ex2(__uint_as_float(s[2 * i]) - m_new);
+          const float c = ex2(__uint_as_float(s[2 * i + 1]) - m_new);
+          sum += a + c;
+          pk[i] = ElemOps<T>::pack2(a, c);
+        }
+        l = l * corr + sum;
+        m = m_new;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = 0u;
+      }
+      tc::tmem_st32(t_s[b] + lane_off, pk);
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar(B_PFULL + b));
+      if (t >= 1 && !accumulate(t - 1, m_prev)) {
+        ok = false;
+        break;
+      }
+      m_prev = m;
+    }
+    if (ok && n_tiles > 0) ok = accumulate(n_tiles - 1, m_prev);
+
+    // ---- epilogue: O / l -> out ----
+    const int64_t qrow = qb0 * 64 + row;
+    const bool valid_row = ok && (half == 0 || has1) && qrow < p.n_tokens;
+    if (valid_row) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* dst = static_cast<T*>(p.out) + (head * p.n_tokens + qrow) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        uint4 v;
+        v.x = ElemOps<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+        v.y = ElemOps<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+        v.z = ElemOps<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+        v.w = ElemOps<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        reinterpret_cast<uint4*>(dst)[c] = v;
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag && p.status) atomicOr(p.status, VGGT_STATUS_TIMEOUT);
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// [heads, rows, 64] tensor of 2-byte elements, box (64, box_rows, 1), 128-B swizzle.
+static bool make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads, int64_t rows,
+                     uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)rows, (cuuint64_t)heads};
+  const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)rows * HD * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)HD, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == VGGT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace tcattn
+
+bool attn_tc05_supported(const AttnArgs& a) {
+  return a.dim == 64 && a.block_q == 64 && a.block_k == 64 && a.n_patch >= 1 &&
+         a.evidence == nullptr && a.nb <= 65536 && a.n_tokens <= 0x7fffffffLL &&
+         a.n_patch <= 0x7fffffffLL && a.n_special <= 0x7fffffffLL && a.heads <= 0x7fffffffLL &&
+         tcattn::encode_fn() != nullptr;
+}
+
+cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
+  using namespace tcattn;
+  if (a.n_slots == 0 || a.qb_count == 0) return cudaSuccess;
+  CUtensorMap mq, mkp, mvp, mks, mvs;
+  const int64_t ns = a.n_special > 0 ? a.n_special : 1;
+  if (!make_map(&mq, a.q, a.dtype, a.heads, a.n_tokens, BM) ||
+      !make_map(&mkp, a.pk, a.dtype, a.heads, a.n_patch, BN) ||
+      !make_map(&mvp, a.pv, a.dtype, a.heads, a.n_patch, BN) ||
+      !make_map(&mks, a.n_special > 0 ? a.sk : a.pk, a.dtype, a.heads,
+                a.n_special > 0 ? ns : a.n_patch, BN) ||
+      !make_map(&mvs, a.n_special > 0 ? a.sv : a.pv, a.dtype, a.heads,
+                a.n_special > 0 ? ns : a.n_patch, BN))
+    return cudaErrorInvalidValue;
+  Params p;
+  p.indices = a.indices;
+  p.counts = a.counts;
+  p.head_ids = a.head_ids;
+  p.head_dense = a.head_dense;
+  p.out = a.out;
+  p.status = a.status;
+  p.heads = a.heads;
+  p.n_tokens = a.n_tokens;
+  p.n_patch = a.n_patch;
+  p.n_special = a.n_special;
+  p.n_slots = a.n_slots;
+  p.max_blocks = a.max_blocks;
+  p.qb_count = a.qb_count;
+  p.nb = a.nb;
+  p.pairs = (a.qb_count + 1) / 2;
+  p.counts_per_qblock = a.counts_per_qblock;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4;
+  const int64_t grid = a.n_slots * p.pairs;
+  if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if (a.dtype == VGGT_DTYPE_BF16) {
+    auto k = attn_tc05_kernel<__nv_bfloat16>;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mq, mkp, mvp, mks, mvs, p);
+  } else {
+    auto k = attn_tc05_kernel<__half>;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mq, mkp, mvp, mks, mvs, p);
+  }
+  return cudaGetLastError();
+}
 
 }  // namespace vggt
