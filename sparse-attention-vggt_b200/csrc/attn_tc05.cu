@@ -13,11 +13,14 @@
 //    [heads, rows, 64], 128-byte swizzle, zero fill past the end of a head)
 //    into a 4-stage ring; warp 1 (one lane) issues the MMAs
 //      S_t  = Q K_t^T  (SS, 128x64x64, fp32 in TMEM, double-buffered)
-//      PV_t = P_t V_t  (TS: P read from TMEM where it overwrote S_t)
+//      O   += P_t V_t  (TS: P read from TMEM where it overwrote S_t; O stays
+//                       in TMEM for the whole key sweep)
 //    and warps 2-5 (128 threads, one query row each) run the softmax: read
-//    S_t, mask, exp2 with the running max, write P_t (bf16/fp16) back to TMEM,
-//    then fold PV_{t-1} into a register accumulator with the exact rescale
-//    factor exp2(m_old - m_new).
+//    S_t, mask tail columns, exp2(s * scale * log2 e - m_ref) with one FFMA
+//    per element, write P_t (bf16/fp16) back to TMEM.  The per-row reference
+//    max m_ref only moves when a tile's max exceeds it by more than 8 in the
+//    exp2 domain; O (in TMEM) and the row sum are rescaled then, so P <= 2^8
+//    and the rescale is rare after the first tiles.
 //  * dense-profiled slots walk every patch block (no index reads): the dense
 //    path of the same kernel.
 //
@@ -44,7 +47,7 @@ constexpr int NSTAGE = 4;       // K/V ring depth
 constexpr int THREADS = 192;
 constexpr uint32_t TILE_BYTES = BN * HD * 2;  // 8 KB
 constexpr uint32_t Q_BYTES = BM * HD * 2;     // 16 KB
-constexpr uint32_t TMEM_COLS = 256;           // S0 | S1 | PV0 | PV1
+constexpr uint32_t TMEM_COLS = 256;           // S0 | S1 | O | (free): 2 CTAs per SM
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
 
 // shared-memory layout (offsets from a 1024-aligned base)
@@ -58,9 +61,9 @@ constexpr int B_KVFULL = 1;                 // [NSTAGE]
 constexpr int B_KVEMPTY = B_KVFULL + NSTAGE;  // [NSTAGE]
 constexpr int B_SFULL = B_KVEMPTY + NSTAGE;   // [2]
 constexpr int B_PFULL = B_SFULL + 2;          // [2]
-constexpr int B_PVFULL = B_PFULL + 2;         // [2]
-constexpr int B_PVEMPTY = B_PVFULL + 2;       // [2]
-constexpr int B_DRAIN = B_PVEMPTY + 2;        // MMA completion before TMEM release
+constexpr int B_PVDONE = B_PFULL + 2;         // one phase per PV MMA
+constexpr int B_OFULL = B_PVDONE + 1;         // the last PV MMA is done
+constexpr int B_DRAIN = B_OFULL + 1;          // MMA completion before TMEM release
 constexpr int NBAR = B_DRAIN + 1;
 constexpr uint32_t OFF_META = OFF_BAR + NBAR * 8;       // int[NSTAGE]
 constexpr uint32_t OFF_MISC = OFF_META + NSTAGE * 4;    // tmem base, abort, tiles, scratch
@@ -82,6 +85,12 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <typename T>
@@ -170,9 +179,9 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar(B_SFULL + b), 1);
       tc::mbar_init(bar(B_PFULL + b), 128);
-      tc::mbar_init(bar(B_PVFULL + b), 1);
-      tc::mbar_init(bar(B_PVEMPTY + b), 128);
     }
+    tc::mbar_init(bar(B_PVDONE), 1);
+    tc::mbar_init(bar(B_OFULL), 1);
     tc::mbar_init(bar(B_DRAIN), 1);
     misc[1] = 0u;  // abort flag
     tc::mbar_fence_init();
@@ -187,7 +196,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc::tc_fence_after();
   const uint32_t tmem = misc[0];
   const uint32_t t_s[2] = {tmem + 0u, tmem + 64u};
-  const uint32_t t_pv[2] = {tmem + 128u, tmem + 192u};
+  const uint32_t t_o = tmem + 128u;
 
   if (warp == 0) {
     // ================= TMA producer =================
@@ -267,21 +276,19 @@ __global__ void __launch_bounds__(THREADS, 2)
       const uint32_t id_pv = tc::idesc_f16(fmt, 1u, BM, HD);
       const uint64_t qdesc = tc::sw128_desc(base + OFF_Q, 16);
       bool ok = tc::mbar_wait(bar(B_QFULL), 0, abort_flag, WAIT_LIMIT_NS);
+      // O (TMEM) += P_u V_u; the first PV of the CTA initialises O.
       auto issue_pv = [&](int64_t u) -> bool {
         const int bu = (int)(u & 1);
         const int su = (int)(u % NSTAGE);
         if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
           return false;
-        if (u >= 2 && !tc::mbar_wait(bar(B_PVEMPTY + bu), (uint32_t)(((u >> 1) - 1) & 1),
-                                     abort_flag, WAIT_LIMIT_NS))
-          return false;
         tc::tc_fence_after();
         const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES, 8192);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc::mma_ts(t_pv[bu], t_s[bu] + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
-                     kk > 0 ? 1u : 0u);
-        tc::mma_commit(bar(B_PVFULL + bu));
+          tc::mma_ts(t_o, t_s[bu] + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
+                     (u > 0 || kk > 0) ? 1u : 0u);
+        tc::mma_commit(bar(B_PVDONE));
         tc::mma_commit(bar(B_KVEMPTY + su));
         return true;
       };
@@ -305,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           break;
         }
       }
-      if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+      if (ok && n_tiles > 0 && issue_pv(n_tiles - 1)) tc::mma_commit(bar(B_OFULL));
       // every issued MMA must finish before the TMEM columns are released
       tc::mma_commit(bar(B_DRAIN));
       tc::mbar_wait_drain(bar(B_DRAIN), 0, WAIT_LIMIT_NS);
@@ -316,39 +323,22 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int row = sub * 32 + lane;          // 0..127
     const int half = row >> 6;                // which query block of the pair
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, m_acc = -INFINITY, m_prev = -INFINITY;
+    const float c = p.scale_log2;
+    // O accumulates in TMEM against a per-row reference max m_ref (raw score
+    // units).  m_ref moves only when a tile's max exceeds it by more than
+    // 2^8 in the exp2 domain; O and l are rescaled then (P stays <= 256).
+    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-
-    auto accumulate = [&](int64_t u, float m_u) -> bool {
-      const int bu = (int)(u & 1);
-      if (!tc::mbar_wait(bar(B_PVFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
-        return false;
-      tc::tc_fence_after();
-      uint32_t r[32];
-      const float f = (m_acc == m_u) ? 1.f : ex2(m_acc - m_u);
-      tc::tmem_ld32(t_pv[bu] + lane_off, r);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], f, __uint_as_float(r[i]));
-      tc::tmem_ld32(t_pv[bu] + lane_off + 32u, r);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[32 + i] = fmaf(o[32 + i], f, __uint_as_float(r[i]));
-      tc::tc_fence_before();
-      tc::mbar_arrive(bar(B_PVEMPTY + bu));
-      m_acc = m_u;
-      return true;
-    };
 
     for (int64_t t = 0; t < n_tiles; ++t) {
       const int stage = (int)(t % NSTAGE);
       const int b = (int)(t & 1);
-      if (!tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
-                         WAIT_LIMIT_NS) ||
-          !tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1), abort_flag, WAIT_LIMIT_NS)) {
+      bool got = tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
+                               WAIT_LIMIT_NS) &&
+                 tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1), abort_flag,
+                               WAIT_LIMIT_NS);
+      // keep the warp converged for the .sync.aligned TMEM instructions
+      if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
@@ -361,26 +351,60 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tmem_ld32(t_s[b] + lane_off + 32u, s + 32);
       tc::tmem_wait_ld();
       uint32_t pk[32];
-      if (active) {
-        float mloc = -INFINITY;
+      if (active) {  // warp-uniform: a warp's 32 rows belong to one query block
+        if (ncols < BN) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float x = (i < ncols) ? __uint_as_float(s[i]) * p.scale_log2 : -INFINITY;
-          s[i] = __float_as_uint(x);
-          mloc = fmaxf(mloc, x);
+          for (int i = 0; i < BN; ++i)
+            if (i >= ncols) s[i] = __float_as_uint(-INFINITY);
         }
-        const float m_new = fmaxf(m, mloc);
-        const float corr = (m == m_new) ? 1.f : ex2(m - m_new);
-        float sum = 0.f;
+        float mx[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          mx[j] = fmax3(__uint_as_float(s[8 * j]),
+                        fmax3(__uint_as_float(s[8 * j + 1]), __uint_as_float(s[8 * j + 2]),
+                              __uint_as_float(s[8 * j + 3])),
+                        fmax3(__uint_as_float(s[8 * j + 4]), __uint_as_float(s[8 * j + 5]),
+                              fmaxf(__uint_as_float(s[8 * j + 6]), __uint_as_float(s[8 * j + 7]))));
+        const float mloc = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                                 fmaxf(mx[6], mx[7]));
+        const bool grow = (mloc - m_ref) * c > 8.f;   // always true while m_ref = -inf
+        const float m_new = grow ? mloc : m_ref;
+        const float factor = grow ? ex2((m_ref - m_new) * c) : 1.f;  // 0 when m_ref = -inf
+        const bool rescale_o = grow && l > 0.f;  // rows without mass have O == 0
+        l *= factor;
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O must hold every PV issued so far (through tile t-1) before it is
+          // rescaled; PV_t cannot start before P_t is published below.
+          const bool done = tc::mbar_wait(bar(B_PVDONE), (uint32_t)((t - 1) & 1), abort_flag,
+                                          WAIT_LIMIT_NS);
+          if (!__all_sync(0xffffffffu, done)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const float f = rescale_o ? factor : 1.f;
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t r[32];
+            tc::tmem_ld32(t_o + lane_off + 32u * h2, r);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            tc::tmem_st32(t_o + lane_off + 32u * h2, r);
+          }
+        }
+        m_ref = m_new;
+        const float mc = m_ref * c;
+        float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float a = ex2(__uint_as_float(s[2 * i]) - m_new);
-          const float c = ex2(__uint_as_float(s[2 * i + 1]) - m_new);
-          sum += a + c;
-          pk[i] = ElemOps<T>::pack2(a, c);
+          const float a = ex2(fmaf(__uint_as_float(s[2 * i]), c, -mc));
+          const float b2 = ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -mc));
+          sum0 += a;
+          sum1 += b2;
+          pk[i] = ElemOps<T>::pack2(a, b2);
         }
-        l = l * corr + sum;
-        m = m_new;
+        l += sum0 + sum1;
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;
@@ -389,28 +413,40 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(bar(B_PFULL + b));
-      if (t >= 1 && !accumulate(t - 1, m_prev)) {
-        ok = false;
-        break;
-      }
-      m_prev = m;
     }
-    if (ok && n_tiles > 0) ok = accumulate(n_tiles - 1, m_prev);
 
     // ---- epilogue: O / l -> out ----
+    if (ok && n_tiles > 0)
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(bar(B_OFULL), 0, abort_flag, WAIT_LIMIT_NS));
+    tc::tc_fence_after();
     const int64_t qrow = qb0 * 64 + row;
     const bool valid_row = ok && (half == 0 || has1) && qrow < p.n_tokens;
-    if (valid_row) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* dst = static_cast<T*>(p.out) + (head * p.n_tokens + qrow) * HD;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    T* dst = static_cast<T*>(p.out) + (head * p.n_tokens + qrow) * HD;
 #pragma unroll
-      for (int c = 0; c < HD / 8; ++c) {
-        uint4 v;
-        v.x = ElemOps<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-        v.y = ElemOps<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        v.z = ElemOps<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        v.w = ElemOps<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-        reinterpret_cast<uint4*>(dst)[c] = v;
+    for (int h2 = 0; h2 < 2; ++h2) {
+      uint32_t r[32];
+      if (ok && n_tiles > 0) {
+        tc::tmem_ld32(t_o + lane_off + 32u * h2, r);
+        tc::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      if (valid_row) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 v;
+          v.x = ElemOps<T>::pack2(__uint_as_float(r[8 * q4 + 0]) * inv,
+                                  __uint_as_float(r[8 * q4 + 1]) * inv);
+          v.y = ElemOps<T>::pack2(__uint_as_float(r[8 * q4 + 2]) * inv,
+                                  __uint_as_float(r[8 * q4 + 3]) * inv);
+          v.z = ElemOps<T>::pack2(__uint_as_float(r[8 * q4 + 4]) * inv,
+                                  __uint_as_float(r[8 * q4 + 5]) * inv);
+          v.w = ElemOps<T>::pack2(__uint_as_float(r[8 * q4 + 6]) * inv,
+                                  __uint_as_float(r[8 * q4 + 7]) * inv);
+          reinterpret_cast<uint4*>(dst)[h2 * 4 + q4] = v;
+        }
       }
     }
   }
@@ -467,7 +503,7 @@ static bool make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads
 
 bool attn_tc05_supported(const AttnArgs& a) {
   return a.dim == 64 && a.block_q == 64 && a.block_k == 64 && a.n_patch >= 1 &&
-         a.evidence == nullptr && a.nb <= 65536 && a.n_tokens <= 0x7fffffffLL &&
+         a.evidence == nullptr && a.scale > 0.f && a.nb <= 65536 && a.n_tokens <= 0x7fffffffLL &&
          a.n_patch <= 0x7fffffffLL && a.n_special <= 0x7fffffffLL && a.heads <= 0x7fffffffLL &&
          tcattn::encode_fn() != nullptr;
 }
