@@ -9,10 +9,11 @@
 //    blocks' selections; a tile selected by only one block is masked to -inf
 //    for the other block's 64 rows, so every output row sees exactly its own
 //    key set.  This keeps tcgen05 at M=128, its full-rate shape.
-//  * warp 0 (one lane) streams K and V tiles with TMA (3-D tensor maps over
-//    [heads, rows, 64], 128-byte swizzle, zero fill past the end of a head)
-//    into a 4-stage ring; warp 1 (one lane) issues the MMAs
-//      S_t  = Q K_t^T  (SS, 128x64x64, fp32 in TMEM, double-buffered)
+//  * each softmax thread loads its query row once into TMEM (the A operand of
+//    QK^T, 32 columns).  Warp 0 (one lane) streams K and V tiles with TMA
+//    (3-D tensor maps over [heads, rows, 64], 128-byte swizzle, zero fill past
+//    the end of a head) into a 4-stage ring; warp 1 (one lane) issues
+//      S_t  = Q K_t^T  (TS: Q from TMEM, K from smem; fp32 S double-buffered)
 //      O   += P_t V_t  (TS: P read from TMEM where it overwrote S_t; O stays
 //                       in TMEM for the whole key sweep)
 //    and warps 2-5 (128 threads, one query row each) run the softmax: read
@@ -36,6 +37,8 @@
 #include "kernels.h"
 #include "tc05.cuh"
 
+
+
 namespace vggt {
 
 namespace tcattn {
@@ -46,15 +49,17 @@ constexpr int HD = 64;          // head dim
 constexpr int NSTAGE = 4;       // K/V ring depth
 constexpr int THREADS = 192;
 constexpr uint32_t TILE_BYTES = BN * HD * 2;  // 8 KB
-constexpr uint32_t Q_BYTES = BM * HD * 2;     // 16 KB
-constexpr uint32_t TMEM_COLS = 256;           // S0 | S1 | O | (free): 2 CTAs per SM
+constexpr uint32_t TMEM_COLS = 256;  // S0 | S1 | O (64 + 16 row-sum cols) | Q: 2 CTAs/SM
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
 
 // shared-memory layout (offsets from a 1024-aligned base)
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+constexpr uint32_t OFF_K = 0;
 constexpr uint32_t OFF_V = OFF_K + NSTAGE * TILE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + NSTAGE * TILE_BYTES;
+// A 64x64 tile of ones, read as N columns 64..79 of the PV MMA's B operand:
+// O[:, 64] then accumulates the row sum of P on the tensor core.
+constexpr uint32_t OFF_ONES = OFF_V + NSTAGE * TILE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_ONES + TILE_BYTES;
+constexpr int ON = 80;  // PV MMA N: 64 value columns + 16 ones columns
 // barrier indices
 constexpr int B_QFULL = 0;
 constexpr int B_KVFULL = 1;                 // [NSTAGE]
@@ -70,6 +75,7 @@ constexpr uint32_t OFF_MISC = OFF_META + NSTAGE * 4;    // tmem base, abort, til
 constexpr uint32_t OFF_BITMAP = (OFF_MISC + 64 + 15) & ~15u;
 
 struct Params {
+  const void* q;
   const int32_t* indices;
   const int32_t* counts;
   const int32_t* head_ids;
@@ -87,6 +93,72 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA/ALU pipes, for x <= 8 (the lazy-rescale bound).  Range
+// reduction x = n + f with n = round(x) (adding 1.5 * 2^23 leaves round(x) in
+// the low mantissa bits), f in [-1/2, 1/2]; 2^f by a cubic fitted to minimise
+// the maximum relative error on that interval (iteratively reweighted least
+// squares, max relative error 7.5e-5, below bf16/fp16 resolution); the result
+// exponent is then advanced by n with one integer add.  x is clamped at -126
+// so the exponent field stays valid (2^-126 is negligible next to P <= 2^8).
+#ifndef VGGT_TC_POLY_PAIRS
+#define VGGT_TC_POLY_PAIRS 0x01u
+#endif
+#ifndef VGGT_TC_EXP_F16X2
+#define VGGT_TC_EXP_F16X2 0
+#endif
+// column pairs (of every 8) whose exponentials run on the FMA pipe
+constexpr unsigned kPolyPairs = VGGT_TC_POLY_PAIRS;
+
+// (d0, d1) = (a0, a1) * b + c with one packed f32x2 FMA
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float n = __fsub_rn(t, 12582912.f);
+  const float f = __fsub_rn(x, n);
+  float q = fmaf(f, 0.05517131f, 0.24261053f);
+  q = fmaf(q, f, 0.69326099f);
+  q = fmaf(q, f, 0.99992811f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+// two polynomial exponentials, packed into the MMA element type
+template <typename T>
+__device__ __forceinline__ uint32_t exp2_poly_pair(float xa, float xb) {
+  return ElemOps<T>::pack2(exp2_poly(xa), exp2_poly(xb));
+}
+
+// two MUFU exponentials, packed into the MMA element type.  With
+// VGGT_TC_EXP_F16X2 the pair is rounded to f16 (11-bit significand; for the
+// x <= 8 range here the argument error is <= 2^-8) and one ex2.f16x2 computes
+// both; otherwise two fp32 ex2.
+template <typename T>
+__device__ __forceinline__ uint32_t exp2_mufu_pair(float xa, float xb) {
+#if VGGT_TC_EXP_F16X2
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(xb), "f"(xa));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  if constexpr (std::is_same<T, __half>::value) {
+    return e;
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<__half2*>(&e));
+    return ElemOps<T>::pack2(f.x, f.y);
+  }
+#else
+  return ElemOps<T>::pack2(ex2(xa), ex2(xb));
+#endif
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -95,8 +167,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 2)
-    attn_tc05_kernel(const __grid_constant__ CUtensorMap tm_q,
-                     const __grid_constant__ CUtensorMap tm_kp,
+    attn_tc05_kernel(const __grid_constant__ CUtensorMap tm_kp,
                      const __grid_constant__ CUtensorMap tm_vp,
                      const __grid_constant__ CUtensorMap tm_ks,
                      const __grid_constant__ CUtensorMap tm_vs, Params p) {
@@ -171,7 +242,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 
   // ---- barriers and TMEM ----
   if (tid == 0) {
-    tc::mbar_init(bar(B_QFULL), 1);
+    tc::mbar_init(bar(B_QFULL), 128);
     for (int s = 0; s < NSTAGE; ++s) {
       tc::mbar_init(bar(B_KVFULL + s), 1);
       tc::mbar_init(bar(B_KVEMPTY + s), 1);
@@ -185,6 +256,13 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc::mbar_init(bar(B_DRAIN), 1);
     misc[1] = 0u;  // abort flag
     tc::mbar_fence_init();
+  }
+  {
+    // ones tile (1.0 in the element type); made visible to the tensor core below
+    const uint32_t one2 = ElemOps<T>::pack2(1.f, 1.f);
+    uint4* ones = reinterpret_cast<uint4*>(sbase + OFF_ONES);
+    for (int i = tid; i < (int)(TILE_BYTES / 16); i += THREADS)
+      ones[i] = make_uint4(one2, one2, one2, one2);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
@@ -195,17 +273,16 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = misc[0];
-  const uint32_t t_s[2] = {tmem + 0u, tmem + 64u};
+  // S buffer b lives at columns [64 b, 64 b + 64)
+  auto t_s_of = [tmem](int b) { return tmem + (uint32_t)(b << 6); };
   const uint32_t t_o = tmem + 128u;
+  const uint32_t t_q = tmem + 208u;  // Q tile as the A operand of QK (32 cols)
 
   if (warp == 0) {
     // ================= TMA producer =================
     if (lane == 0) {
-      tc::prefetch_tmap(&tm_q);
       tc::prefetch_tmap(&tm_kp);
       tc::prefetch_tmap(&tm_vp);
-      tc::mbar_expect_tx(bar(B_QFULL), Q_BYTES);
-      tc::tma_load_3d(base + OFF_Q, &tm_q, bar(B_QFULL), 0, (int)(qb0 * 64), (int)head);
       int wi = 0;
       uint32_t cur = 0, curA = 0;
       if (!dense && nwords > 0) {
@@ -273,8 +350,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (lane == 0) {
       const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       const uint32_t id_qk = tc::idesc_f16(fmt, 0u, BM, BN);
-      const uint32_t id_pv = tc::idesc_f16(fmt, 1u, BM, HD);
-      const uint64_t qdesc = tc::sw128_desc(base + OFF_Q, 16);
+      const uint32_t id_pv = tc::idesc_f16(fmt, 1u, BM, ON);
       bool ok = tc::mbar_wait(bar(B_QFULL), 0, abort_flag, WAIT_LIMIT_NS);
       // O (TMEM) += P_u V_u; the first PV of the CTA initialises O.
       auto issue_pv = [&](int64_t u) -> bool {
@@ -283,10 +359,12 @@ __global__ void __launch_bounds__(THREADS, 2)
         if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
           return false;
         tc::tc_fence_after();
-        const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES, 8192);
+        // MN group 0 = the V tile, group 1 (LBO bytes further) = the ones tile
+        const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES,
+                                              OFF_ONES - (OFF_V + su * TILE_BYTES));
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc::mma_ts(t_o, t_s[bu] + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
+          tc::mma_ts(t_o, t_s_of(bu) + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
                      (u > 0 || kk > 0) ? 1u : 0u);
         tc::mma_commit(bar(B_PVDONE));
         tc::mma_commit(bar(B_KVEMPTY + su));
@@ -304,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         const uint64_t kdesc = tc::sw128_desc(base + OFF_K + stage * TILE_BYTES, 16);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          tc::mma_ss(t_s[b], qdesc + (uint64_t)(kk * 2), kdesc + (uint64_t)(kk * 2), id_qk,
+          tc::mma_ts(t_s_of(b), t_q + (uint32_t)(kk * 8), kdesc + (uint64_t)(kk * 2), id_qk,
                      kk > 0 ? 1u : 0u);
         tc::mma_commit(bar(B_SFULL + b));
         if (t >= 1 && !issue_pv(t - 1)) {
@@ -324,11 +402,33 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int half = row >> 6;                // which query block of the pair
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const float c = p.scale_log2;
+    {
+      // this thread's query row -> TMEM (A operand layout: 2 elements per column)
+      const int64_t qrow = qb0 * 64 + row;
+      uint32_t r[32];
+      if (qrow < p.n_tokens) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
+                                                          (head * p.n_tokens + qrow) * HD);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint4 v = __ldg(src + k);
+          r[4 * k] = v.x; r[4 * k + 1] = v.y; r[4 * k + 2] = v.z; r[4 * k + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) r[k] = 0u;
+      }
+      tc::tmem_st32(t_q + lane_off, r);
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar(B_QFULL));
+    }
     // O accumulates in TMEM against a per-row reference max m_ref (raw score
     // units).  m_ref moves only when a tile's max exceeds it by more than
-    // 2^8 in the exp2 domain; O and l are rescaled then (P stays <= 256).
-    float m_ref = -INFINITY, l = 0.f;
-    bool ok = true;
+    // 2^8 in the exp2 domain; O (value and row-sum columns) is rescaled then
+    // (P stays <= 256).
+    float m_ref = -INFINITY;
+    bool has_mass = false, ok = true;
 
     for (int64_t t = 0; t < n_tiles; ++t) {
       const int stage = (int)(t % NSTAGE);
@@ -347,8 +447,8 @@ __global__ void __launch_bounds__(THREADS, 2)
       const bool active = (mt >> half) & 1;
       tc::tc_fence_after();
       uint32_t s[64];
-      tc::tmem_ld32(t_s[b] + lane_off, s);
-      tc::tmem_ld32(t_s[b] + lane_off + 32u, s + 32);
+      tc::tmem_ld32(t_s_of(b) + lane_off, s);
+      tc::tmem_ld32(t_s_of(b) + lane_off + 32u, s + 32);
       tc::tmem_wait_ld();
       uint32_t pk[32];
       if (active) {  // warp-uniform: a warp's 32 rows belong to one query block
@@ -370,8 +470,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         const bool grow = (mloc - m_ref) * c > 8.f;   // always true while m_ref = -inf
         const float m_new = grow ? mloc : m_ref;
         const float factor = grow ? ex2((m_ref - m_new) * c) : 1.f;  // 0 when m_ref = -inf
-        const bool rescale_o = grow && l > 0.f;  // rows without mass have O == 0
-        l *= factor;
+        const bool rescale_o = grow && has_mass;  // rows without mass have O == 0
         if (__any_sync(0xffffffffu, rescale_o)) {
           // O must hold every PV issued so far (through tile t-1) before it is
           // rescaled; PV_t cannot start before P_t is published below.
@@ -392,24 +491,43 @@ __global__ void __launch_bounds__(THREADS, 2)
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
             tc::tmem_st32(t_o + lane_off + 32u * h2, r);
           }
+          {  // the row-sum column
+            uint32_t r[8];
+            tc::tmem_ld8(t_o + lane_off + 64u, r);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            tc::tmem_st8(t_o + lane_off + 64u, r);
+          }
         }
         m_ref = m_new;
+        has_mass = true;
         const float mc = m_ref * c;
-        float sum0 = 0.f, sum1 = 0.f;
+        if (ncols < BN) {
+          // tail tile: masked columns are -inf, which the MUFU path maps to 0
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = ex2(fmaf(__uint_as_float(s[2 * i]), c, -mc));
-          const float b2 = ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -mc));
-          sum0 += a;
-          sum1 += b2;
-          pk[i] = ElemOps<T>::pack2(a, b2);
+          for (int i = 0; i < 32; ++i)
+            pk[i] = ElemOps<T>::pack2(ex2(fmaf(__uint_as_float(s[2 * i]), c, -mc)),
+                                      ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -mc)));
+        } else {
+          // full tile: x = s * c - m_ref * c two columns at a time (f32x2
+          // FMA); the column pairs selected by kPolyPairs go through the
+          // FMA-pipe polynomial, the rest through MUFU, to balance the pipes
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float xa, xb;
+            ffma2(xa, xb, __uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]), c, -mc);
+            if ((kPolyPairs >> (i & 7)) & 1u)
+              pk[i] = exp2_poly_pair<T>(xa, xb);
+            else
+              pk[i] = exp2_mufu_pair<T>(xa, xb);
+          }
         }
-        l += sum0 + sum1;
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;
       }
-      tc::tmem_st32(t_s[b] + lane_off, pk);
+      tc::tmem_st32(t_s_of(b) + lane_off, pk);
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(bar(B_PFULL + b));
@@ -421,6 +539,13 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc::tc_fence_after();
     const int64_t qrow = qb0 * 64 + row;
     const bool valid_row = ok && (half == 0 || has1) && qrow < p.n_tokens;
+    float l = 0.f;
+    if (ok && n_tiles > 0) {
+      uint32_t r[8];
+      tc::tmem_ld8(t_o + lane_off + 64u, r);
+      tc::tmem_wait_ld();
+      l = __uint_as_float(r[0]);
+    }
     const float inv = l > 0.f ? 1.f / l : 0.f;
     T* dst = static_cast<T*>(p.out) + (head * p.n_tokens + qrow) * HD;
 #pragma unroll
@@ -511,10 +636,9 @@ bool attn_tc05_supported(const AttnArgs& a) {
 cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   using namespace tcattn;
   if (a.n_slots == 0 || a.qb_count == 0) return cudaSuccess;
-  CUtensorMap mq, mkp, mvp, mks, mvs;
+  CUtensorMap mkp, mvp, mks, mvs;
   const int64_t ns = a.n_special > 0 ? a.n_special : 1;
-  if (!make_map(&mq, a.q, a.dtype, a.heads, a.n_tokens, BM) ||
-      !make_map(&mkp, a.pk, a.dtype, a.heads, a.n_patch, BN) ||
+  if (!make_map(&mkp, a.pk, a.dtype, a.heads, a.n_patch, BN) ||
       !make_map(&mvp, a.pv, a.dtype, a.heads, a.n_patch, BN) ||
       !make_map(&mks, a.n_special > 0 ? a.sk : a.pk, a.dtype, a.heads,
                 a.n_special > 0 ? ns : a.n_patch, BN) ||
@@ -522,6 +646,7 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
                 a.n_special > 0 ? ns : a.n_patch, BN))
     return cudaErrorInvalidValue;
   Params p;
+  p.q = a.q;
   p.indices = a.indices;
   p.counts = a.counts;
   p.head_ids = a.head_ids;
@@ -547,12 +672,12 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
     auto k = attn_tc05_kernel<__nv_bfloat16>;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k<<<(unsigned)grid, THREADS, smem, stream>>>(mq, mkp, mvp, mks, mvs, p);
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mkp, mvp, mks, mvs, p);
   } else {
     auto k = attn_tc05_kernel<__half>;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k<<<(unsigned)grid, THREADS, smem, stream>>>(mq, mkp, mvp, mks, mvs, p);
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mkp, mvp, mks, mvs, p);
   }
   return cudaGetLastError();
 }
