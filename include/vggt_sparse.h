@@ -116,6 +116,32 @@ int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int6
                              int32_t* status, void* stream);
 
 /*
+ * vggt_block_mask_estimate without the pooled_q / pooled_k scratch arguments.
+ * No counterpart in the reference (it exists for callers of this C ABI that
+ * cannot allocate device memory: code that runs where cudaMalloc is not
+ * allowed, or whose device memory is planned once at start-up).  The pooled
+ * rows go to a fixed 8 MiB array inside the library instead; every GPU that
+ * loads the library holds that array until the process exits.
+ *
+ * Inputs, outputs and results are those of vggt_block_mask_estimate.  The
+ * call allocates nothing.  It fails (negative return, message in
+ * vggt_sparse_last_error) when
+ *   n_slots * (ceil(n_tokens/block_q) + ceil(n_patch/block_k)) * dim * 4
+ * exceeds 8 MiB (e.g. 16 heads x 43,968 tokens x 64 dims needs 5.6 MiB).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the one array: calls whose
+ * work can overlap on the GPU (other streams, other threads) race on it and
+ * must be serialised by the caller.
+ */
+int vggt_block_mask_estimate_noalloc(const void* q, const void* patch_k, int dtype, int64_t heads,
+                                     int64_t n_tokens, int64_t n_patch, int dim,
+                                     const int32_t* head_ids, int64_t n_slots, int block_q,
+                                     int block_k, int mode, int64_t topk, double tau, float scale,
+                                     int32_t* indices, int64_t max_blocks, int32_t* counts,
+                                     float* scores, int32_t* status, void* stream);
+
+/*
  * Selection only, from caller-supplied fp32 pooled scores [rows, n_blocks]
  * (row-major).  Used to re-run the selection rule on exported scores.
  */

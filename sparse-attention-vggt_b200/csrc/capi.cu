@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -193,3 +194,72 @@ int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int m
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Estimator without caller-provided scratch.
+//
+// The estimator needs a temporary buffer for the pooled (block-mean) Q and K
+// rows.  Some callers cannot hand one over: code running where no allocator
+// may be called (inside a driver or plugin callback that forbids
+// cudaMalloc, a runtime that pre-plans all device memory up front, or a
+// host that is not allowed to grow GPU memory after start-up).  For them the
+// pooled rows live in this fixed array in the library's own device memory.
+// Every GPU that loads the library reserves it until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB of fp32 pooled rows
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {};  // device address of the array, per device
+std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array on the current device.  The host-side
+// name g_noalloc_scratch is only a stand-in for the symbol, never a device
+// pointer, so the address is looked up once per device and cached.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_rc(e);
+  if (dev < 0 || dev >= kMaxDevices) return fail("device ordinal %d not supported", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_rc(e);
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int vggt_block_mask_estimate_noalloc(
+    const void* q, const void* patch_k, int dtype, int64_t heads, int64_t n_tokens,
+    int64_t n_patch, int dim, const int32_t* head_ids, int64_t n_slots, int block_q, int block_k,
+    int mode, int64_t topk, double tau, float scale, int32_t* indices, int64_t max_blocks,
+    int32_t* counts, float* scores, int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  float* pooled_q = nullptr;
+  float* pooled_k = nullptr;
+  if (block_q > 0 && block_k > 0 && dim > 0 && n_tokens >= 0 && n_patch >= 0 && n_slots > 0 &&
+      n_slots <= 65535) {
+    const int64_t rows = cdiv(n_tokens, block_q) + cdiv(n_patch, block_k);
+    const int64_t cap = (int64_t)(kNoAllocScratchBytes / sizeof(float));
+    if (rows > cap / dim / n_slots)
+      return fail("pooled rows need %lld bytes; the built-in scratch holds %lld bytes "
+                  "(n_slots * (ceil(n_tokens/block_q) + ceil(n_patch/block_k)) * dim * 4)",
+                  (long long)(n_slots * rows * dim * 4), (long long)kNoAllocScratchBytes);
+    const int rc = noalloc_scratch(&pooled_q);
+    if (rc) return rc;
+    // both halves start on a 16-byte boundary: dim is a multiple of 32
+    pooled_k = pooled_q + n_slots * cdiv(n_tokens, block_q) * dim;
+  }
+  // The pooling kernels write every pooled element they later read, so the
+  // array's contents left by an earlier call never need clearing.
+  return vggt_block_mask_estimate(q, patch_k, dtype, heads, n_tokens, n_patch, dim, head_ids,
+                                  n_slots, block_q, block_k, mode, topk, tau, scale, pooled_q,
+                                  pooled_k, indices, max_blocks, counts, scores, status, stream);
+}

@@ -27,6 +27,9 @@ SIGNATURES = {
                                       ctypes.c_double, ctypes.c_float, _P, _P, _P, _I64, _P, _P, _P,
                                       _P]),
     "vggt_block_select": (_I, [_P, _I64, _I64, _I, _I64, ctypes.c_double, _P, _I64, _P, _P]),
+    "vggt_block_mask_estimate_noalloc": (_I, [_P, _P, _I, _I64, _I64, _I64, _I, _P, _I64, _I, _I,
+                                              _I, _I64, ctypes.c_double, ctypes.c_float, _P, _I64,
+                                              _P, _P, _P, _P]),
 }
 
 

@@ -27,8 +27,8 @@ def lib():
 
 def test_header_declares_the_documented_entry_points():
     assert declared_symbols() == sorted([
-        "vggt_block_attention", "vggt_block_mask_estimate", "vggt_block_select",
-        "vggt_sparse_last_error", "vggt_sparse_version"])
+        "vggt_block_attention", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
+        "vggt_block_select", "vggt_sparse_last_error", "vggt_sparse_version"])
 
 
 def test_library_exports_every_declared_symbol(lib):
