@@ -62,6 +62,19 @@ def load_peaks():
         return dict(FALLBACK_PEAKS)
 
 
+def profiled_traffic(config):
+    """DRAM bytes (read + write) per attention launch from the committed ncu
+    summary of this workload, or None when no summary exists."""
+    import re
+    path = os.path.join(REPO, "profiles", "attn_tc05_%s.md" % config)
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic per launch \(read \+ write\) \| ([0-9.]+) MB", text)
+    return float(m.group(1)) * 1e6 if m else None
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -371,7 +384,9 @@ def main():
         "estimator_ms": est_local, "attention_ms": att_local,
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": att_tflops / peaks["bf16_tflops"], "traffic": None,
+                     "frac": att_tflops / peaks["bf16_tflops"],
+                     "traffic": profiled_traffic(args.config),
+                     "traffic_unit": "bytes per launch (dram read + write, from profiles/)",
                      "flops_per_launch": flops_local,
                      "peak_source": peaks["source"] + " bf16 burst"},
         "estimator_roofline": {"bound": "hbm", "achieved": est_bytes / (est_local * 1e-3) / 1e9,
