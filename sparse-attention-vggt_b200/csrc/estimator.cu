@@ -91,29 +91,45 @@ __global__ void __launch_bounds__(256) pool_blocks_kernel(const T* __restrict__ 
 // Radix select of one row by one warp.
 // ---------------------------------------------------------------------------
 struct SelectHist {
-  unsigned long long w[256];
-  unsigned int c[256];
+  unsigned long long w[256];  // per-digit weight (top-k: count) of the candidates
 };
 
 __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
   return (key & 0x80000000u) ? (key & 0x7fffffffu) : ~key;
 }
 
-// Writes ascending selected ids (and -1 padding) to out[0:max_blocks]; returns m.
-__device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode, int64_t topk,
-                               uint64_t tau_num, SelectHist* hist, int32_t* __restrict__ out,
+// Selects one row of fp32 scores held in shared memory.  The row is
+// overwritten with the monotone uint32 keys of its scores; for the mass rule
+// wrow receives each block's quantised softmax weight.  Writes ascending
+// selected ids (and -1 padding) to out[0:max_blocks]; returns their count m.
+__device__ int select_row_warp(float* __restrict__ srow, unsigned long long* __restrict__ wrow,
+                               int nb, int mode, int64_t topk, uint64_t tau_num,
+                               SelectHist* hist, int32_t* __restrict__ out,
                                int64_t max_blocks) {
   const int lane = threadIdx.x & 31;
   const unsigned full = 0xffffffffu;
   const unsigned lt_mask = (1u << lane) - 1u;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(srow);
+  const bool mass = mode == VGGT_SELECT_MASS;
   float rowmax = -INFINITY;
   uint64_t target, total;
-  if (mode == VGGT_SELECT_MASS) {
+  if (mass) {
     for (int i = lane; i < nb; i += 32) rowmax = fmaxf(rowmax, srow[i]);
 #pragma unroll
     for (int off = 16; off; off >>= 1) rowmax = fmaxf(rowmax, __shfl_xor_sync(full, rowmax, off));
-    unsigned long long tw = 0;
-    for (int i = lane; i < nb; i += 32) tw += det_mass_weight(srow[i], rowmax);
+  }
+  // keys (and weights) once per element
+  unsigned long long tw = 0;
+  for (int i = lane; i < nb; i += 32) {
+    const float sc = srow[i];
+    if (mass) {
+      const unsigned long long w = det_mass_weight(sc, rowmax);
+      wrow[i] = w;
+      tw += w;
+    }
+    keys[i] = score_key(sc);
+  }
+  if (mass) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) tw += __shfl_xor_sync(full, tw, off);
     total = tw;
@@ -122,59 +138,47 @@ __device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode,
     total = (uint64_t)nb;
     target = (uint64_t)(topk < (int64_t)nb ? topk : (int64_t)nb);
   }
+  __syncwarp();
 
   int m;
   // Every block is kept when k >= nb, or when no prefix reaches the mass target
   // (m = #(cum < T) + 1 then exceeds nb and is clamped).  A mass target equal to
   // the total still goes through the radix path: trailing zero-weight blocks
   // are excluded exactly as the reference's cumsum would exclude them.
-  if (target > total || (mode == VGGT_SELECT_TOPK && target == total)) {
+  if (target > total || (!mass && target == total)) {
     m = nb;
     for (int i = lane; i < nb; i += 32)
       if (i < max_blocks) out[i] = i;
   } else {
     uint32_t prefix = 0, prefix_mask = 0;
     unsigned long long above_w = 0;
-    unsigned int above_c = 0;
 #pragma unroll 1
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = lane; b < 256; b += 32) {
-        hist->w[b] = 0ull;
-        hist->c[b] = 0u;
-      }
+      for (int bnum = lane; bnum < 256; bnum += 32) hist->w[bnum] = 0ull;
       __syncwarp();
       for (int i = lane; i < nb; i += 32) {
-        const float s = srow[i];
-        const uint32_t key = score_key(s);
-        if ((key & prefix_mask) == prefix) {
-          const int dgt = (key >> shift) & 255;
-          const unsigned long long w =
-              (mode == VGGT_SELECT_MASS) ? (unsigned long long)det_mass_weight(s, rowmax) : 1ull;
-          atomicAdd(&hist->w[dgt], w);
-          atomicAdd(&hist->c[dgt], 1u);
-        }
+        const uint32_t key = keys[i];
+        if ((key & prefix_mask) == prefix)
+          atomicAdd(&hist->w[(key >> shift) & 255], mass ? wrow[i] : 1ull);
       }
       __syncwarp();
-      // lane L owns digits 8L .. 8L+7
+      // lane L owns digits 8L .. 8L+7; find the highest digit whose suffix
+      // weight (plus everything already above the prefix) reaches the target
       unsigned long long lw[8];
-      unsigned int lc[8];
       unsigned long long lane_w = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         lw[j] = hist->w[8 * lane + j];
-        lc[j] = hist->c[8 * lane + j];
         lane_w += lw[j];
       }
-      // exclusive suffix sum over higher lanes
       unsigned long long suffix = lane_w;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        unsigned long long v = __shfl_down_sync(full, suffix, off);
+        const unsigned long long v = __shfl_down_sync(full, suffix, off);
         if (lane + off < 32) suffix += v;
       }
-      unsigned long long above_lane = suffix - lane_w;  // digits of higher lanes
       int found = -1;
-      unsigned long long run = above_w + above_lane;
+      unsigned long long run = above_w + (suffix - lane_w);
 #pragma unroll
       for (int j = 7; j >= 0; --j) {
         if (found < 0) {
@@ -184,44 +188,24 @@ __device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode,
       }
       const unsigned ball = __ballot_sync(full, found >= 0);
       const int win = 31 - __clz(ball);  // highest lane holding a qualifying digit
-      // winner: run = above_w + weight of digits strictly above the found one
-      unsigned long long new_above_w = run;
-      unsigned int cnt_above = 0;
-      if (lane == win) {
-        // count of digits strictly above `found` inside this lane
-        for (int j = 7; j > found; --j) cnt_above += lc[j];
-      }
-      // counts of higher lanes
-      unsigned int lane_c = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) lane_c += lc[j];
-      unsigned int csuffix = lane_c;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        unsigned int v = __shfl_down_sync(full, csuffix, off);
-        if (lane + off < 32) csuffix += v;
-      }
-      cnt_above += csuffix - lane_c;
       const int digit = __shfl_sync(full, 8 * lane + found, win);
-      above_w = __shfl_sync(full, new_above_w, win);
-      above_c += __shfl_sync(full, cnt_above, win);
+      above_w = __shfl_sync(full, run, win);
       prefix |= (uint32_t)digit << shift;
       prefix_mask |= 255u << shift;
       __syncwarp();
     }
-    // prefix is now the key of the last selected element
+    // prefix is now the key of the last selected element; take enough of its
+    // ties (lowest ids first) to reach the target
     unsigned long long tie_w = 1ull;
-    if (mode == VGGT_SELECT_MASS) tie_w = det_mass_weight(__uint_as_float(key_to_bits(prefix)), rowmax);
+    if (mass) tie_w = det_mass_weight(__uint_as_float(key_to_bits(prefix)), rowmax);
     const unsigned long long need = target - above_w;  // > 0
     const unsigned int ties_taken = (unsigned int)((need + tie_w - 1ull) / tie_w);
-    m = (int)(above_c + ties_taken);
-    // compaction in id order
+    // compaction in id order; m is the number written
     unsigned int tie_seen = 0, written = 0;
     for (int base = 0; base < nb; base += 32) {
       const int i = base + lane;
-      uint32_t key = 0;
-      bool valid = i < nb;
-      if (valid) key = score_key(srow[i]);
+      const bool valid = i < nb;
+      const uint32_t key = valid ? keys[i] : 0u;
       const bool gt = valid && key > prefix;
       const bool eq = valid && key == prefix;
       const unsigned eqb = __ballot_sync(full, eq);
@@ -233,6 +217,7 @@ __device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode,
       written += __popc(incb);
       tie_seen += __popc(eqb);
     }
+    m = (int)written;
   }
   for (int64_t j = m + lane; j < max_blocks; j += 32) out[j] = -1;
   return m;
@@ -243,20 +228,21 @@ __device__ int select_row_warp(const float* __restrict__ srow, int nb, int mode,
 // Q rows and their complete fp32 score rows live in shared memory; pooled K
 // is streamed once per CTA.  Warps then select rows independently.
 // ---------------------------------------------------------------------------
-template <int D, bool FROM_SCORES>
-__global__ void __launch_bounds__(256) score_select_kernel(
+template <int D, bool FROM_SCORES, int RMAX>
+__global__ void __launch_bounds__(256, 3) score_select_kernel(
     const float* __restrict__ pooled_q, const float* __restrict__ pooled_k, int64_t qb_count,
-    int64_t nb, int rows_per_cta, float scale, int mode, int64_t topk, uint64_t tau_num,
+    int64_t nb, float scale, int mode, int64_t topk, uint64_t tau_num,
     int32_t* __restrict__ indices, int64_t max_blocks, int32_t* __restrict__ counts,
     float* __restrict__ scores_out, const float* __restrict__ scores_in) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  SelectHist* hist = reinterpret_cast<SelectHist*>(smem_raw);  // [8]
-  float* qbar = reinterpret_cast<float*>(hist + 8);           // [R][D]
-  float* srows = qbar + (FROM_SCORES ? 0 : rows_per_cta * D); // [R][nb]
+  SelectHist* hist = reinterpret_cast<SelectHist*>(smem_raw);                // [8]
+  unsigned long long* wrows = reinterpret_cast<unsigned long long*>(hist + 8);  // [RMAX][nb]
+  float* qbar = reinterpret_cast<float*>(wrows + (mode == VGGT_SELECT_MASS ? RMAX * nb : 0));
+  float* srows = qbar + (FROM_SCORES ? 0 : RMAX * D);                       // [RMAX][nb]
 
   const int64_t slot = blockIdx.y;
-  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
-  const int rows = (int)(qb_count - r0 < rows_per_cta ? qb_count - r0 : rows_per_cta);
+  const int64_t r0 = (int64_t)blockIdx.x * RMAX;
+  const int rows = (int)(qb_count - r0 < RMAX ? qb_count - r0 : RMAX);
   const int tid = threadIdx.x;
 
   if constexpr (FROM_SCORES) {
@@ -268,24 +254,37 @@ __global__ void __launch_bounds__(256) score_select_kernel(
   } else {
     const float* qsrc = pooled_q + (slot * qb_count + r0) * D;
     for (int i = tid; i < rows * D; i += blockDim.x) qbar[i] = qsrc[i];
+    for (int i = rows * D + tid; i < RMAX * D; i += blockDim.x) qbar[i] = 0.f;
     __syncthreads();
     const float* ksrc = pooled_k + slot * nb * D;
     for (int64_t kb = tid; kb < nb; kb += blockDim.x) {
-      float kv[D];
+      // every row's dot product accumulates d = 0 .. D-1 in order (one fmaf
+      // each); pooled K is streamed in 16-float chunks to keep registers low
+      float acc[RMAX];
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) acc[r] = 0.f;
       const float4* kp = reinterpret_cast<const float4*>(ksrc + kb * D);
 #pragma unroll
-      for (int i = 0; i < D / 4; ++i) {
-        float4 t = __ldg(kp + i);
-        kv[4 * i] = t.x; kv[4 * i + 1] = t.y; kv[4 * i + 2] = t.z; kv[4 * i + 3] = t.w;
-      }
-      for (int r = 0; r < rows; ++r) {
-        const float* qr = qbar + r * D;
-        float acc = 0.f;
+      for (int i0 = 0; i0 < D; i0 += 16) {
+        float kv[16];
 #pragma unroll
-        for (int i = 0; i < D; ++i) acc = fmaf(qr[i], kv[i], acc);
-        const float s = acc * scale;
-        srows[r * nb + kb] = s;
-        if (scores_out) scores_out[(slot * qb_count + r0 + r) * nb + kb] = s;
+        for (int i = 0; i < 4; ++i) {
+          const float4 t = __ldg(kp + i0 / 4 + i);
+          kv[4 * i] = t.x; kv[4 * i + 1] = t.y; kv[4 * i + 2] = t.z; kv[4 * i + 3] = t.w;
+        }
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[r] = fmaf(qbar[r * D + i0 + j], kv[j], acc[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < rows) {
+          const float sc = acc[r] * scale;
+          srows[r * nb + kb] = sc;
+          if (scores_out) scores_out[(slot * qb_count + r0 + r) * nb + kb] = sc;
+        }
       }
     }
   }
@@ -293,8 +292,8 @@ __global__ void __launch_bounds__(256) score_select_kernel(
   const int warp = tid >> 5;
   for (int r = warp; r < rows; r += (blockDim.x >> 5)) {
     const int64_t row = slot * qb_count + r0 + r;
-    int m = select_row_warp(srows + (int64_t)r * nb, (int)nb, mode, topk, tau_num, hist + warp,
-                            indices + row * max_blocks, max_blocks);
+    int m = select_row_warp(srows + (int64_t)r * nb, wrows + (int64_t)r * nb, (int)nb, mode, topk,
+                            tau_num, hist + warp, indices + row * max_blocks, max_blocks);
     if ((threadIdx.x & 31) == 0) counts[row] = m;
   }
 }
@@ -302,42 +301,51 @@ __global__ void __launch_bounds__(256) score_select_kernel(
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
-static int select_rows_per_cta(int64_t nb, int d, int64_t qb_count, bool from_scores) {
-  const int64_t budget = 200 * 1024 - 8 * (int64_t)sizeof(SelectHist);
-  const int64_t per_row = nb * 4 + (from_scores ? 0 : d * 4);
-  int64_t r = budget / per_row;
-  r = std::min<int64_t>(r, 32);
-  r = std::min<int64_t>(r, qb_count);
-  return (int)r;
+// Shared memory of one selection CTA holding `rows` score rows.
+static size_t select_smem_bytes(int rows, int64_t nb, int d, bool from_scores, bool mass) {
+  return 8 * sizeof(SelectHist) + (size_t)rows * ((from_scores ? 0 : d) + nb) * 4 +
+         (mass ? (size_t)rows * nb * 8 : 0);
+}
+constexpr size_t kSelectSmemBudget = 220 * 1024;
+
+template <int D, bool FROM, int RMAX>
+static cudaError_t launch_select_r(const float* pq, const float* pk, int64_t qb_count, int64_t nb,
+                                   int64_t n_slots, float scale, int mode, int64_t topk,
+                                   uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                   int32_t* counts, float* scores_out, const float* scores_in,
+                                   cudaStream_t stream) {
+  const size_t smem = select_smem_bytes(RMAX, nb, D, FROM, mode == VGGT_SELECT_MASS);
+  auto kern = score_select_kernel<D, FROM, RMAX>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((qb_count + RMAX - 1) / RMAX), (unsigned)n_slots);
+  kern<<<grid, 256, smem, stream>>>(pq, pk, qb_count, nb, scale, mode, topk, tau_num, indices,
+                                     max_blocks, counts, scores_out, scores_in);
+  return cudaGetLastError();
 }
 
-static size_t select_smem_bytes(int rows, int64_t nb, int d, bool from_scores) {
-  return 8 * sizeof(SelectHist) + (size_t)rows * ((from_scores ? 0 : d) + nb) * 4;
-}
-
+// 8 query-block rows per CTA (one warp each) when they fit in shared memory,
+// else 2 (very long rows).
 template <int D, bool FROM>
 static cudaError_t launch_select_t(const float* pq, const float* pk, int64_t qb_count, int64_t nb,
                                    int64_t n_slots, float scale, int mode, int64_t topk,
                                    uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                    int32_t* counts, float* scores_out, const float* scores_in,
                                    cudaStream_t stream) {
-  const int rows = select_rows_per_cta(nb, D, qb_count, FROM);
-  if (rows < 1) return cudaErrorInvalidValue;
-  const size_t smem = select_smem_bytes(rows, nb, D, FROM);
-  auto kern = score_select_kernel<D, FROM>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((qb_count + rows - 1) / rows), (unsigned)n_slots);
-  kern<<<grid, 256, smem, stream>>>(pq, pk, qb_count, nb, rows, scale, mode, topk, tau_num,
-                                     indices, max_blocks, counts, scores_out, scores_in);
-  return cudaGetLastError();
+  const bool mass = mode == VGGT_SELECT_MASS;
+  if (select_smem_bytes(8, nb, D, FROM, mass) <= kSelectSmemBudget)
+    return launch_select_r<D, FROM, 8>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                       indices, max_blocks, counts, scores_out, scores_in, stream);
+  if (select_smem_bytes(2, nb, D, FROM, mass) <= kSelectSmemBudget)
+    return launch_select_r<D, FROM, 2>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                       indices, max_blocks, counts, scores_out, scores_in, stream);
+  return cudaErrorInvalidValue;
 }
 
 int estimator_max_blocks_supported(int d) {
-  // largest nb with at least one row per CTA
-  const int64_t budget = 200 * 1024 - 8 * (int64_t)sizeof(SelectHist);
-  return (int)(budget / 4 - d);
+  // largest nb that still fits two rows per CTA with mass weights
+  return (int)((kSelectSmemBudget - 8 * sizeof(SelectHist)) / (2 * 12) - d);
 }
 
 template <typename T>
