@@ -42,7 +42,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", default="cfg2")
-    p.add_argument("--shard", choices=("qblocks", "heads"), default="qblocks")
+    p.add_argument("--shard", choices=("qblocks", "heads", "kv-allgather"), default="qblocks")
     p.add_argument("--kernel", default="auto")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -172,24 +172,22 @@ class ClockSampler:
 
 
 def shard_inputs(x, cfg, rank, world, shard, device):
-    """Per-rank slice of the layer.  qblocks: contiguous query-block range,
-    all heads; heads: contiguous head range, all tokens."""
+    """Per-rank slice of the layer.  qblocks / kv-allgather: a contiguous range
+    of 64-row query blocks, all heads; heads: a cost-balanced set of heads
+    (dense-profiled heads spread out), all tokens."""
     if world == 1:
         return x.q, x.kp, x.vp, x.ks, x.vs, list(cfg.dense_heads), (0, x.shape.n_tokens)
-    if shard == "qblocks":
-        qbc = x.shape.n_qblocks
-        per = math.ceil(qbc / world)
-        b0, b1 = rank * per, min(qbc, (rank + 1) * per)
+    from vggt_sparse import distributed as vd
+    if shard in ("qblocks", "kv-allgather"):
+        b0, b1 = vd.qblock_range(x.shape.n_qblocks, world, rank)
         r0, r1 = b0 * cfg.block, min(x.shape.n_tokens, b1 * cfg.block)
         q = x.q[:, r0:r1].contiguous()
         return q, x.kp, x.vp, x.ks, x.vs, list(cfg.dense_heads), (r0, r1)
-    h = cfg.heads
-    per = math.ceil(h / world)
-    h0, h1 = rank * per, min(h, (rank + 1) * per)
-    sl = slice(h0, h1)
-    dense = [d - h0 for d in cfg.dense_heads if h0 <= d < h1]
-    return (x.q[sl].contiguous(), x.kp[sl].contiguous(), x.vp[sl].contiguous(),
-            x.ks[sl].contiguous(), x.vs[sl].contiguous(), dense, (0, x.shape.n_tokens))
+    mine = vd.head_assignment(cfg.heads, world, cfg.dense_heads)[rank]
+    idx = torch.tensor(mine, device=device)
+    dense = [i for i, h in enumerate(mine) if h in set(cfg.dense_heads)]
+    sel = [t.index_select(0, idx).contiguous() for t in (x.q, x.kp, x.vp, x.ks, x.vs)]
+    return (*sel, dense, (0, x.shape.n_tokens))
 
 
 def cpu_baseline(cfg, x_cpu, sample_blocks):
@@ -289,12 +287,31 @@ def main():
     flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
     launches_per_step = (3 if layer.sparse_heads else 0) + 1
 
+    gather = None
+    if args.shard == "kv-allgather" and world > 1:
+        # each rank holds the K/V of its own frames; one NCCL all-gather per
+        # tensor (inside every timed step) rebuilds the layer's full K/V
+        from vggt_sparse import distributed as vd
+        f0, f1 = vd.frame_range(cfg.frames, world, rank)
+        ppf, spf = x.shape.patch_h * x.shape.patch_w, x.shape.special_per_frame
+        local = [x.kp[:, f0 * ppf:f1 * ppf].contiguous(), x.vp[:, f0 * ppf:f1 * ppf].contiguous(),
+                 x.ks[:, f0 * spf:f1 * spf].contiguous(), x.vs[:, f0 * spf:f1 * spf].contiguous()]
+
+        def gather():
+            return [vd.allgather_frames(t, world) for t in local]
+
+    def step(events=None):
+        if events is not None:
+            events[0].record()
+        kv = gather() if gather is not None else (kp, vp, ks, vs)
+        layer(q, *kv, out=out, events=None if events is None else events[1:])
+
     for _ in range(args.warmup):
-        layer(q, kp, vp, ks, vs, out=out)
+        step()
     torch.cuda.synchronize()
     flops_local = layer.kept_flops(q.shape[1], kp.shape[1], ks.shape[1], q.shape[2])
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     sampler = ClockSampler(device.index) if rank == 0 else None
     barrier(world)
     torch.cuda.synchronize()
@@ -302,13 +319,14 @@ def main():
         sampler.start()
     for i in range(args.steps):
         flush.zero_()
-        layer(q, kp, vp, ks, vs, out=out, events=ev[i])
+        step(ev[i])
     torch.cuda.synchronize()
     barrier(world)
     clocks = sampler.stop() if sampler else None
-    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
-    est_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    att_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    step_ms = [e[0].elapsed_time(e[3]) for e in ev]
+    gather_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    est_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    att_ms = [e[2].elapsed_time(e[3]) for e in ev]
     ms_local = sum(step_ms) / len(step_ms)
     ms = reduce_max(ms_local, world)
     att_local = sum(att_ms) / len(att_ms)
@@ -382,6 +400,7 @@ def main():
         "kept_block_gflop_per_layer": flops_total / 1e9,
         "frames_per_s": cfg.frames / (ms * 1e-3),
         "estimator_ms": est_local, "attention_ms": att_local,
+        "allgather_ms": (sum(gather_ms) / len(gather_ms)) if gather is not None else None,
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": att_tflops / peaks["bf16_tflops"],

@@ -1,0 +1,108 @@
+"""Partitioning one global-attention layer over the GPUs of a box.
+
+One process per GPU (``torch.distributed``, NCCL over NVLink).  The reference
+runs one process per GPU on whole scenes and has no intra-layer partitioning
+(SAF3R shards scenes across GPUs with CUDA_VISIBLE_DEVICES, e.g.
+scripts/run_scannet50_all_gpus.sh:9); the layouts here are new:
+
+* query-block sharding: rank r owns a contiguous range of 64-row query blocks
+  (all heads).  With the layer's K/V replicated on every rank nothing crosses
+  NVLink inside the layer; with K/V sharded by frames (each rank computed
+  only its own tokens' K/V) one all-gather of K and V precedes the layer.
+* head sharding: rank r owns a set of heads (all tokens), balanced by cost so
+  dense-profiled heads are spread out.  No collective inside attention.
+"""
+import math
+
+import torch
+
+from .layer import SparseGlobalLayer
+
+
+def qblock_range(n_qblocks, world, rank):
+    """[b0, b1) query blocks of `rank`; ranges are contiguous and cover all blocks."""
+    per = math.ceil(n_qblocks / world)
+    b0 = min(n_qblocks, rank * per)
+    return b0, min(n_qblocks, b0 + per)
+
+
+def head_assignment(n_heads, world, dense_heads=(), sparse_cost=0.3):
+    """Heads per rank, greedy longest-first by cost (dense head = 1.0, sparse =
+    ``sparse_cost``), each rank's list ascending.  Ties go to the lower rank."""
+    dense = set(int(h) for h in dense_heads)
+    order = sorted(range(n_heads), key=lambda h: (-(1.0 if h in dense else sparse_cost), h))
+    load = [0.0] * world
+    out = [[] for _ in range(world)]
+    for h in order:
+        r = min(range(world), key=lambda i: (load[i], len(out[i]), i))
+        out[r].append(h)
+        load[r] += 1.0 if h in dense else sparse_cost
+    return [sorted(x) for x in out]
+
+
+def frame_range(frames, world, rank):
+    """[f0, f1) frames whose tokens rank `rank` owns under frame sharding."""
+    per = math.ceil(frames / world)
+    f0 = min(frames, rank * per)
+    return f0, min(frames, f0 + per)
+
+
+def allgather_frames(local, world, group=None):
+    """All-gather a frame-sharded [H, n_local, d] tensor into [H, world * n_local, d].
+
+    Every rank must hold the same n_local (frames divisible by world).  One
+    all-gather over NCCL (gloo on CPU) lands the shards rank-major in a
+    [world, H, n_local, d] buffer; one copy reorders them head-major, which is
+    the layout the attention kernels read."""
+    import torch.distributed as dist
+    h, n, d = local.shape
+    buf = torch.empty((world, h, n, d), device=local.device, dtype=local.dtype)
+    dist.all_gather_into_tensor(buf.view(-1), local.contiguous().view(-1), group=group)
+    return buf.permute(1, 0, 2, 3).reshape(h, world * n, d)
+
+
+class QBlockShardedLayer:
+    """The layer restricted to this rank's query blocks.
+
+    ``__call__(q, kp, vp, ks, vs)`` takes the FULL q (or only this rank's rows
+    when ``q_is_local``) and full K/V; it returns this rank's output rows
+    [H, rows, d] and their global row range."""
+
+    def __init__(self, heads, world, rank, **layer_kwargs):
+        self.world, self.rank = world, rank
+        self.layer = SparseGlobalLayer(heads, **layer_kwargs)
+
+    def rows(self, n_tokens):
+        b0, b1 = qblock_range(math.ceil(n_tokens / self.layer.block), self.world, self.rank)
+        return b0 * self.layer.block, min(n_tokens, b1 * self.layer.block)
+
+    def __call__(self, q, kp, vp, ks, vs, n_tokens=None, q_is_local=False, out=None):
+        n = n_tokens if n_tokens is not None else q.shape[1]
+        r0, r1 = self.rows(n)
+        if self.layer.mode == "topk" and self.layer.topk is None:
+            # the budget follows the FULL layer, as the reference computes it
+            from .layer import topk_budget
+            nb = math.ceil(kp.shape[1] / self.layer.block)
+            self.layer.topk = topk_budget(self.layer.retention, n, ks.shape[1], nb,
+                                          self.layer.block)
+        ql = q if q_is_local else q[:, r0:r1].contiguous()
+        return self.layer(ql, kp, vp, ks, vs, out=out), (r0, r1)
+
+
+class HeadShardedLayer:
+    """The layer restricted to this rank's heads (``head_assignment``)."""
+
+    def __init__(self, heads, world, rank, dense_heads=(), **layer_kwargs):
+        self.heads = head_assignment(heads, world, dense_heads)[rank]
+        local_dense = [i for i, h in enumerate(self.heads) if h in set(dense_heads)]
+        self.layer = SparseGlobalLayer(len(self.heads), dense_heads=local_dense, **layer_kwargs)
+
+    def __call__(self, q, kp, vp, ks, vs, out=None):
+        idx = torch.tensor(self.heads, device=q.device)
+        sel = [t.index_select(0, idx).contiguous() for t in (q, kp, vp, ks, vs)]
+        if self.layer.mode == "topk" and self.layer.topk is None:
+            from .layer import topk_budget
+            nb = math.ceil(kp.shape[1] / self.layer.block)
+            self.layer.topk = topk_budget(self.layer.retention, q.shape[1], ks.shape[1], nb,
+                                          self.layer.block)
+        return self.layer(*sel, out=out), self.heads
