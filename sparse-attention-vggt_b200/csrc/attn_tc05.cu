@@ -72,7 +72,10 @@ constexpr int B_DRAIN = B_OFULL + 1;          // MMA completion before TMEM rele
 constexpr int NBAR = B_DRAIN + 1;
 constexpr uint32_t OFF_META = OFF_BAR + NBAR * 8;       // int[NSTAGE]
 constexpr uint32_t OFF_MISC = OFF_META + NSTAGE * 4;    // tmem base, abort, tiles, scratch
-constexpr uint32_t OFF_BITMAP = (OFF_MISC + 64 + 15) & ~15u;
+// evidence partials: float[4 ring][2 query blocks][2 warps] + int counters[4][2]
+constexpr uint32_t OFF_EV = (OFF_MISC + 64 + 15) & ~15u;
+constexpr uint32_t OFF_BITMAP = OFF_EV + 4 * 2 * 2 * 4 + 4 * 2 * 4;
+// (bitmaps, then for evidence the uint16 slot index of each block per query block)
 
 struct Params {
   const void* q;
@@ -83,6 +86,7 @@ struct Params {
   void* out;
   int32_t* status;
   int64_t heads, n_tokens, n_patch, n_special, n_slots, max_blocks, qb_count, nb, pairs;
+  float* evidence;  // [n_slots, qb_count, max_blocks] or null
   int counts_per_qblock;
   float scale_log2;
 };
@@ -165,7 +169,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <typename T>
+template <typename T, bool EVID>
 __global__ void __launch_bounds__(THREADS, 2)
     attn_tc05_kernel(const __grid_constant__ CUtensorMap tm_kp,
                      const __grid_constant__ CUtensorMap tm_vp,
@@ -199,6 +203,11 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int nwords = (int)((p.nb + 31) >> 5);
   uint32_t* bmA = bm;
   uint32_t* bmB = bm + nwords;
+  // slot of each selected block in its query block's index list (evidence only)
+  uint16_t* invA = reinterpret_cast<uint16_t*>(bm + 2 * nwords);
+  uint16_t* invB = invA + ((p.nb + 7) & ~7LL);
+  float* ev_part = reinterpret_cast<float*>(sbase + OFF_EV);
+  int* ev_cnt = reinterpret_cast<int*>(ev_part + 16);
 
   // ---- union of the two query blocks' selections as two bitmaps ----
   int64_t n_patch_tiles;
@@ -220,13 +229,21 @@ __global__ void __launch_bounds__(THREADS, 2)
     bool bad = false;
     for (int64_t i = tid; i < c0; i += THREADS) {
       const int32_t kb = row0[i];
-      if (kb >= 0 && kb < p.nb) atomicOr(&bmA[kb >> 5], 1u << (kb & 31));
-      else bad = true;
+      if (kb >= 0 && kb < p.nb) {
+        atomicOr(&bmA[kb >> 5], 1u << (kb & 31));
+        if (EVID) invA[kb] = (uint16_t)i;
+      } else {
+        bad = true;
+      }
     }
     for (int64_t i = tid; i < c1; i += THREADS) {
       const int32_t kb = row1[i];
-      if (kb >= 0 && kb < p.nb) atomicOr(&bmB[kb >> 5], 1u << (kb & 31));
-      else bad = true;
+      if (kb >= 0 && kb < p.nb) {
+        atomicOr(&bmB[kb >> 5], 1u << (kb & 31));
+        if (EVID) invB[kb] = (uint16_t)i;
+      } else {
+        bad = true;
+      }
     }
     if (bad && p.status) atomicOr(p.status, VGGT_STATUS_BAD_INDEX);
     __syncthreads();
@@ -255,6 +272,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc::mbar_init(bar(B_OFULL), 1);
     tc::mbar_init(bar(B_DRAIN), 1);
     misc[1] = 0u;  // abort flag
+    for (int i = 0; i < 8; ++i) ev_cnt[i] = 0;
     tc::mbar_fence_init();
   }
   {
@@ -328,7 +346,11 @@ __global__ void __launch_bounds__(THREADS, 2)
           mv = &tm_vs;
         }
         if (t == n_tiles - 1) flags |= 4;
-        meta[stage] = flags | (ncols << 8);
+        const bool special = t >= n_patch_tiles;
+        // bits 0-1 query-block flags, 2 last, 3 special, 4-10 valid columns,
+        // 12-31 patch block id
+        meta[stage] = flags | (special ? 8 : 0) | (ncols << 4) |
+                      ((special ? 0 : row / BN) << 12);
         tc::mbar_expect_tx(bar(B_KVFULL + stage), 2 * TILE_BYTES);
         tc::tma_load_3d(base + OFF_K + stage * TILE_BYTES, mk, bar(B_KVFULL + stage), 0, row,
                         (int)head);
@@ -443,7 +465,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         break;
       }
       const int mt = meta[stage];
-      const int ncols = (mt >> 8) & 0xff;
+      const int ncols = (mt >> 4) & 0x7f;
       const bool active = (mt >> half) & 1;
       tc::tc_fence_after();
       uint32_t s[64];
@@ -503,7 +525,44 @@ __global__ void __launch_bounds__(THREADS, 2)
         m_ref = m_new;
         has_mass = true;
         const float mc = m_ref * c;
-        if (ncols < BN) {
+        if constexpr (EVID) {
+          // Same-pass evidence (adaptive_block_attention.py:29-33): the row's
+          // log-sum-exp over this tile's keys, from the fp32 weights of the
+          // same exponentials (all on MUFU here), averaged over the query
+          // block's valid rows.  The two warps of a query block combine their
+          // partial sums through shared memory; the second one stores.
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float xa, xb;
+            ffma2(xa, xb, __uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]), c, -mc);
+            const float ea = ex2(xa), eb = ex2(xb);
+            sum += ea + eb;
+            pk[i] = ElemOps<T>::pack2(ea, eb);
+          }
+          if (!(mt & 8) && !dense) {  // patch tiles of indexed slots only
+            const int64_t qrow = qb0 * 64 + row;
+            float v = qrow < p.n_tokens ? (mc + __log2f(sum)) * 0.6931471805599453f : 0.f;
+#pragma unroll
+            for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) {
+              const int slotr = (int)(t & 3) * 2 + half;
+              ev_part[slotr * 2 + (sub & 1)] = v;
+              __threadfence_block();
+              if (atomicAdd(&ev_cnt[slotr], 1) == 1) {
+                __threadfence_block();
+                const float tot = ev_part[slotr * 2] + ev_part[slotr * 2 + 1];
+                ev_cnt[slotr] = 0;
+                const int64_t qb = qb0 + half;
+                const int64_t nvalid =
+                    p.n_tokens - qb * 64 < 64 ? p.n_tokens - qb * 64 : 64;
+                const int kb = (int)((unsigned)mt >> 12);
+                const int j = half ? invB[kb] : invA[kb];
+                p.evidence[(slot * p.qb_count + qb) * p.max_blocks + j] = tot / (float)nvalid;
+              }
+            }
+          }
+        } else if (ncols < BN) {
           // tail tile: masked columns are -inf, which the MUFU path maps to 0
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -628,9 +687,21 @@ static bool make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads
 
 bool attn_tc05_supported(const AttnArgs& a) {
   return a.dim == 64 && a.block_q == 64 && a.block_k == 64 && a.n_patch >= 1 &&
-         a.evidence == nullptr && a.scale > 0.f && a.nb <= 65536 && a.n_tokens <= 0x7fffffffLL &&
+         a.scale > 0.f && a.nb <= 65536 && a.max_blocks <= 65536 && a.n_tokens <= 0x7fffffffLL &&
          a.n_patch <= 0x7fffffffLL && a.n_special <= 0x7fffffffLL && a.heads <= 0x7fffffffLL &&
          tcattn::encode_fn() != nullptr;
+}
+
+template <typename T, bool EVID>
+static cudaError_t launch_kernel(int64_t grid, size_t smem, cudaStream_t stream,
+                                 const CUtensorMap& mkp, const CUtensorMap& mvp,
+                                 const CUtensorMap& mks, const CUtensorMap& mvs,
+                                 const tcattn::Params& p) {
+  auto k = tcattn::attn_tc05_kernel<T, EVID>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<(unsigned)grid, tcattn::THREADS, smem, stream>>>(mkp, mvp, mks, mvs, p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
@@ -663,22 +734,21 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   p.nb = a.nb;
   p.pairs = (a.qb_count + 1) / 2;
   p.counts_per_qblock = a.counts_per_qblock;
+  p.evidence = a.evidence;
   p.scale_log2 = a.scale * 1.4426950408889634f;
-  const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4;
+  const bool evid = a.evidence != nullptr;
+  const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4 +
+                      (evid ? 2 * (size_t)((a.nb + 7) & ~7LL) * 2 : 0);
   const int64_t grid = a.n_slots * p.pairs;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   cudaError_t e;
-  if (a.dtype == VGGT_DTYPE_BF16) {
-    auto k = attn_tc05_kernel<__nv_bfloat16>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k<<<(unsigned)grid, THREADS, smem, stream>>>(mkp, mvp, mks, mvs, p);
-  } else {
-    auto k = attn_tc05_kernel<__half>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k<<<(unsigned)grid, THREADS, smem, stream>>>(mkp, mvp, mks, mvs, p);
-  }
+  if (a.dtype == VGGT_DTYPE_BF16)
+    e = evid ? launch_kernel<__nv_bfloat16, true>(grid, smem, stream, mkp, mvp, mks, mvs, p)
+             : launch_kernel<__nv_bfloat16, false>(grid, smem, stream, mkp, mvp, mks, mvs, p);
+  else
+    e = evid ? launch_kernel<__half, true>(grid, smem, stream, mkp, mvp, mks, mvs, p)
+             : launch_kernel<__half, false>(grid, smem, stream, mkp, mvp, mks, mvs, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

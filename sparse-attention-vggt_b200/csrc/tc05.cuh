@@ -203,6 +203,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       VGGT_W8(0), VGGT_W8(8), VGGT_W8(16), VGGT_W8(24)
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      VGGT_W8(0), VGGT_W8(8)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : VGGT_R8(0)

@@ -22,7 +22,7 @@ from vggt_sparse.synthetic import clustered_layer
 pytestmark = pytest.mark.gpu
 
 KERNELS = ["mma_sync", "tcgen05"]
-EVIDENCE_KERNELS = {"mma_sync"}
+EVIDENCE_KERNELS = {"mma_sync", "tcgen05"}
 
 
 def _supported(kernel, d, bq, bk):
