@@ -116,17 +116,43 @@ def reduce_sum(x, world):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock / throttle sampling while the timed region runs.
+
+    nvidia-smi takes a few hundred ms to emit its first row, longer than a
+    short timed loop, so `start()` returns only once samples are flowing and
+    every row carries a timestamp: `stop()` keeps the rows taken between
+    `mark_begin()` and `mark_end()` (plus the first row after the end, so a
+    loop shorter than the sampling period still has one sample)."""
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 20
 
     def __init__(self, device_index):
         self.proc = None
         self.path = None
         self.device_index = device_index
+        self.t_begin = self.t_end = None
 
-    def start(self):
+    def _rows(self):
+        import datetime
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) < 10:
+                        continue
+                    try:
+                        ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                    except ValueError:
+                        continue
+                    rows.append((ts.timestamp(), parts[1:]))
+        except OSError:
+            pass
+        return rows
+
+    def start(self, ready_timeout_s=10.0):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -137,13 +163,32 @@ class ClockSampler:
             except Exception:
                 pass
             cmd = ["nvidia-smi", "--query-gpu=" + self.QUERY, "--format=csv,noheader,nounits",
-                   "-lms", "50"]
+                   "-lms", str(self.PERIOD_MS)]
             if bus:
                 cmd += ["--id=" + bus]
             self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        deadline = time.time() + ready_timeout_s
+        while time.time() < deadline and not self._rows() and self.proc.poll() is None:
+            time.sleep(0.02)
+
+    def mark_begin(self):
+        self.t_begin = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+        if self.proc is None:
+            return
+        # wait (bounded) for the first row stamped after the timed region
+        deadline = time.time() + 1.0
+        while time.time() < deadline and self.proc.poll() is None:
+            rows = self._rows()
+            if rows and rows[-1][0] >= self.t_end:
+                break
+            time.sleep(self.PERIOD_MS / 1000.0)
 
     def stop(self):
         if self.proc is None:
@@ -153,13 +198,14 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+        rows = self._rows()
         os.unlink(self.path)
+        if self.t_begin is not None and self.t_end is not None:
+            inside = [r for t, r in rows if self.t_begin <= t <= self.t_end]
+            after = [r for t, r in rows if t > self.t_end][:1]
+            rows = inside + after
+        else:
+            rows = [r for _, r in rows]
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -317,10 +363,16 @@ def main():
     torch.cuda.synchronize()
     if sampler:
         sampler.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_begin()
     for i in range(args.steps):
         flush.zero_()
         step(ev[i])
     torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_end()
     barrier(world)
     clocks = sampler.stop() if sampler else None
     step_ms = [e[0].elapsed_time(e[3]) for e in ev]
