@@ -314,6 +314,7 @@ def main():
         run_reference_arm(args, rank, world)
         return
     import vggt_sparse
+    from vggt_sparse import ops
     from vggt_sparse.configs import CONFIGS
     from vggt_sparse.synthetic import clustered_layer
     cfg = CONFIGS[args.config]
@@ -331,7 +332,13 @@ def main():
                                              x.shape.n_blocks, cfg.block)
     out = torch.empty_like(q)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
+    # estimator (pool Q, pool K, score + select), query-block pairing (bitmaps,
+    # window costs, greedy) when the tcgen05 kernel runs paired, attention
     launches_per_step = (3 if layer.sparse_heads else 0) + 1
+    if layer.sparse_heads and layer.pair_qblocks and args.kernel != "mma_sync" and \
+            ops.attention_workspace_size(q.shape[1], kp.shape[1], len(layer.sparse_heads) +
+                                         len(layer.dense_heads)) > 0:
+        launches_per_step += 3
 
     gather = None
     if args.shard == "kv-allgather" and world > 1:

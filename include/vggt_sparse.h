@@ -87,6 +87,37 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
                          int32_t* status, int kernel, void* stream);
 
 /*
+ * vggt_block_attention with a scheduling workspace.  No counterpart in the
+ * reference (its Triton kernel runs one 64-row query block per program); the
+ * arguments before `workspace` are those of vggt_block_attention.
+ *
+ * The tcgen05 kernel runs two query blocks per 128-row tile over the union of
+ * their selections.  Given a workspace of at least
+ * vggt_block_attention_workspace_size() bytes (16-byte aligned, device
+ * memory), it first pairs the query blocks of every indexed slot so that the
+ * two selections of a tile differ least (three small kernels on `stream`),
+ * which removes most of the masked tile work; the output is bit-identical
+ * to the unpaired run.  workspace == NULL, or a kernel choice other than
+ * tcgen05, runs exactly vggt_block_attention.  A workspace smaller than the
+ * size query is an argument error.
+ */
+int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patch_v,
+                            const void* special_k, const void* special_v, int dtype,
+                            int64_t heads, int64_t n_tokens, int64_t n_patch, int64_t n_special,
+                            int dim, const int32_t* indices, const int32_t* counts,
+                            int counts_per_qblock, const int32_t* head_ids,
+                            const uint8_t* head_dense, int64_t n_slots, int64_t max_blocks,
+                            int block_q, int block_k, float scale, void* out, float* evidence,
+                            int32_t* status, int kernel, void* stream, void* workspace,
+                            size_t workspace_bytes);
+
+/* Workspace bytes vggt_block_attention_ex needs for query-block pairing (0 when
+ * the shape is not paired: fewer than 2 or more than 65536 query blocks or key
+ * blocks). */
+size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, int64_t n_slots,
+                                           int block_q, int block_k);
+
+/*
  * Block-mask estimator.  Mean-pools q over query blocks of block_q tokens and
  * patch_k over key blocks of block_k tokens (saf3r/patch/adaptive_block_value.py:16-23,
  * applied to both), forms pooled scores S = (Qbar . Kbar^T) * scale in fp32

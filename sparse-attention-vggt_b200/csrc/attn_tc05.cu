@@ -87,6 +87,7 @@ struct Params {
   int32_t* status;
   int64_t heads, n_tokens, n_patch, n_special, n_slots, max_blocks, qb_count, nb, pairs;
   float* evidence;  // [n_slots, qb_count, max_blocks] or null
+  const int32_t* pair_table;  // [indexed slots, pairs, 2] or null
   int counts_per_qblock;
   float scale_log2;
 };
@@ -198,8 +199,17 @@ __global__ void __launch_bounds__(THREADS, 2)
     return;
   }
   const bool dense = p.head_dense != nullptr && p.head_dense[slot] != 0;
-  const int64_t qb0 = 2 * pair, qb1 = qb0 + 1;
-  const bool has1 = qb1 < p.qb_count;
+  // the tile's two query blocks: (2p, 2p + 1), or an entry of the pair table
+  int64_t qb0 = 2 * pair, qb1 = qb0 + 1;
+  if (!dense && p.pair_table != nullptr) {
+    qb0 = p.pair_table[2 * (slot * p.pairs + pair)];
+    qb1 = p.pair_table[2 * (slot * p.pairs + pair) + 1];
+    if (qb0 < 0 || qb0 >= p.qb_count || qb1 < -1 || qb1 >= p.qb_count || qb1 == qb0) {
+      if (tid == 0 && p.status) atomicOr(p.status, VGGT_STATUS_BAD_INDEX);
+      return;
+    }
+  }
+  const bool has1 = qb1 >= 0 && qb1 < p.qb_count;
   const int nwords = (int)((p.nb + 31) >> 5);
   uint32_t* bmA = bm;
   uint32_t* bmB = bm + nwords;
@@ -225,7 +235,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (tid == 0) misc[2] = 0u;
     __syncthreads();
     const int32_t* row0 = p.indices + (slot * p.qb_count + qb0) * p.max_blocks;
-    const int32_t* row1 = row0 + p.max_blocks;
+    const int32_t* row1 = p.indices + (slot * p.qb_count + (has1 ? qb1 : qb0)) * p.max_blocks;
     bool bad = false;
     for (int64_t i = tid; i < c0; i += THREADS) {
       const int32_t kb = row0[i];
@@ -422,13 +432,14 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int sub = warp & 3;                 // TMEM lane quarter of this warp
     const int row = sub * 32 + lane;          // 0..127
     const int half = row >> 6;                // which query block of the pair
+    const int64_t my_qb = half ? (has1 ? qb1 : -1) : qb0;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const float c = p.scale_log2;
     {
       // this thread's query row -> TMEM (A operand layout: 2 elements per column)
-      const int64_t qrow = qb0 * 64 + row;
+      const int64_t qrow = my_qb * 64 + (row & 63);
       uint32_t r[32];
-      if (qrow < p.n_tokens) {
+      if (my_qb >= 0 && qrow < p.n_tokens) {
         const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
                                                           (head * p.n_tokens + qrow) * HD);
 #pragma unroll
@@ -541,8 +552,8 @@ __global__ void __launch_bounds__(THREADS, 2)
             pk[i] = ElemOps<T>::pack2(ea, eb);
           }
           if (!(mt & 8) && !dense) {  // patch tiles of indexed slots only
-            const int64_t qrow = qb0 * 64 + row;
-            float v = qrow < p.n_tokens ? (mc + __log2f(sum)) * 0.6931471805599453f : 0.f;
+            const int64_t qrow = my_qb * 64 + (row & 63);
+            float v = my_qb >= 0 && qrow < p.n_tokens ? (mc + __log2f(sum)) * 0.6931471805599453f : 0.f;
 #pragma unroll
             for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
             if (lane == 0) {
@@ -553,7 +564,7 @@ __global__ void __launch_bounds__(THREADS, 2)
                 __threadfence_block();
                 const float tot = ev_part[slotr * 2] + ev_part[slotr * 2 + 1];
                 ev_cnt[slotr] = 0;
-                const int64_t qb = qb0 + half;
+                const int64_t qb = my_qb;
                 const int64_t nvalid =
                     p.n_tokens - qb * 64 < 64 ? p.n_tokens - qb * 64 : 64;
                 const int kb = (int)((unsigned)mt >> 12);
@@ -596,8 +607,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (ok && n_tiles > 0)
       ok = __all_sync(0xffffffffu, tc::mbar_wait(bar(B_OFULL), 0, abort_flag, WAIT_LIMIT_NS));
     tc::tc_fence_after();
-    const int64_t qrow = qb0 * 64 + row;
-    const bool valid_row = ok && (half == 0 || has1) && qrow < p.n_tokens;
+    const int64_t qrow = my_qb * 64 + (row & 63);
+    const bool valid_row = ok && my_qb >= 0 && qrow < p.n_tokens;
     float l = 0.f;
     if (ok && n_tiles > 0) {
       uint32_t r[8];
@@ -735,6 +746,7 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   p.pairs = (a.qb_count + 1) / 2;
   p.counts_per_qblock = a.counts_per_qblock;
   p.evidence = a.evidence;
+  p.pair_table = a.qblock_pairs;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   const bool evid = a.evidence != nullptr;
   const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4 +

@@ -43,13 +43,24 @@ int vggt_sparse_version(void) { return (1 << 16) | 0; }
 
 const char* vggt_sparse_last_error(void) { return g_err; }
 
-int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v,
-                         const void* special_k, const void* special_v, int dtype, int64_t heads,
-                         int64_t n_tokens, int64_t n_patch, int64_t n_special, int dim,
-                         const int32_t* indices, const int32_t* counts, int counts_per_qblock,
-                         const int32_t* head_ids, const uint8_t* head_dense, int64_t n_slots,
-                         int64_t max_blocks, int block_q, int block_k, float scale, void* out,
-                         float* evidence, int32_t* status, int kernel, void* stream) {
+size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, int64_t n_slots,
+                                          int block_q, int block_k) {
+  if (n_tokens <= 0 || n_patch <= 0 || n_slots <= 0 || block_q <= 0 || block_k <= 0) return 0;
+  const int64_t qb = cdiv(n_tokens, block_q), nb = cdiv(n_patch, block_k);
+  if (!vggt::qblock_pairing_supported(qb, nb)) return 0;
+  return vggt::qblock_pairing_workspace(n_slots, qb, nb) +
+         (((size_t)n_slots * cdiv(qb, 2) * 2 * 4 + 255) & ~(size_t)255);
+}
+
+int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patch_v,
+                            const void* special_k, const void* special_v, int dtype,
+                            int64_t heads, int64_t n_tokens, int64_t n_patch, int64_t n_special,
+                            int dim, const int32_t* indices, const int32_t* counts,
+                            int counts_per_qblock, const int32_t* head_ids,
+                            const uint8_t* head_dense, int64_t n_slots, int64_t max_blocks,
+                            int block_q, int block_k, float scale, void* out, float* evidence,
+                            int32_t* status, int kernel, void* stream, void* workspace,
+                            size_t workspace_bytes) {
   g_err[0] = '\0';
   if (dtype != VGGT_DTYPE_BF16 && dtype != VGGT_DTYPE_FP16)
     return fail("Tensor-core sparse execution requires BF16 or FP16 (dtype code %d)", dtype);
@@ -103,14 +114,46 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
   a.dtype = dtype;
   a.counts_per_qblock = counts_per_qblock ? 1 : 0;
   a.scale = scale;
+  a.qblock_pairs = nullptr;
   if (a.qb_count > 0x7fffffffLL) return fail("too many query blocks");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc_ok = vggt::attn_tc05_supported(a);
   if (kernel == VGGT_ATTN_TCGEN05 && !tc_ok)
     return fail("tcgen05 kernel does not support this shape (needs dim 64, block_q 64, block_k 64)");
-  if (kernel == VGGT_ATTN_TCGEN05 || (kernel == VGGT_ATTN_AUTO && tc_ok))
+  if (kernel == VGGT_ATTN_TCGEN05 || (kernel == VGGT_ATTN_AUTO && tc_ok)) {
+    const size_t need =
+        vggt_block_attention_workspace_size(n_tokens, n_patch, n_slots, block_q, block_k);
+    if (workspace != nullptr && need > 0 && max_blocks > 0) {
+      if (workspace_bytes < need)
+        return fail("workspace of %zu bytes, %zu needed", workspace_bytes, need);
+      if (!aligned16(workspace)) return fail("workspace must be 16-byte aligned");
+      // pair table first, then the pairing scratch
+      int32_t* pairs = static_cast<int32_t*>(workspace);
+      void* scratch = static_cast<unsigned char*>(workspace) +
+                      (((size_t)n_slots * cdiv(a.qb_count, 2) * 2 * 4 + 255) & ~(size_t)255);
+      const cudaError_t e = vggt::launch_qblock_pairing(indices, counts, a.counts_per_qblock,
+                                                        head_dense, n_slots, a.qb_count,
+                                                        max_blocks, a.nb, pairs, scratch, s);
+      if (e != cudaSuccess) return cuda_rc(e);
+      a.qblock_pairs = pairs;
+    }
     return cuda_rc(vggt::launch_attn_tc05(a, s));
+  }
   return cuda_rc(vggt::launch_attn_mma(a, s));
+}
+
+int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v,
+                         const void* special_k, const void* special_v, int dtype, int64_t heads,
+                         int64_t n_tokens, int64_t n_patch, int64_t n_special, int dim,
+                         const int32_t* indices, const int32_t* counts, int counts_per_qblock,
+                         const int32_t* head_ids, const uint8_t* head_dense, int64_t n_slots,
+                         int64_t max_blocks, int block_q, int block_k, float scale, void* out,
+                         float* evidence, int32_t* status, int kernel, void* stream) {
+  return vggt_block_attention_ex(q, patch_k, patch_v, special_k, special_v, dtype, heads,
+                                 n_tokens, n_patch, n_special, dim, indices, counts,
+                                 counts_per_qblock, head_ids, head_dense, n_slots, max_blocks,
+                                 block_q, block_k, scale, out, evidence, status, kernel, stream,
+                                 nullptr, 0);
 }
 
 int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int64_t heads,

@@ -35,11 +35,24 @@ struct AttnArgs {
   const uint8_t* head_dense;
   float* evidence;
   int32_t* status;
+  // [n_indexed_slots, ceil(qb_count / 2), 2] query-block pairs of the
+  // indexed slots (second entry -1 when alone), or null for (2p, 2p + 1)
+  const int32_t* qblock_pairs;
   int64_t heads, n_tokens, n_patch, n_special;
   int64_t n_slots, max_blocks, qb_count, nb;
   int dim, block_q, block_k, dtype, counts_per_qblock;
   float scale;
 };
+
+// pairing.cu: query-block pairing for the 128-row tcgen05 tiles
+constexpr int PAIR_WINDOW = 128;
+size_t qblock_pairing_workspace(int64_t n_slots, int64_t qb_count, int64_t nb);
+bool qblock_pairing_supported(int64_t qb_count, int64_t nb);
+cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
+                                  int counts_per_qblock, const uint8_t* head_dense,
+                                  int64_t n_slots, int64_t qb_count, int64_t max_blocks,
+                                  int64_t nb, int32_t* pairs, void* workspace,
+                                  cudaStream_t stream);
 
 // attn_mma.cu
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);

@@ -42,6 +42,8 @@ class SparseGlobalLayer:
         self.workspace = EstimatorWorkspace()
         self._cache = {}
         self.last_masks = None
+        # pair query blocks by selection overlap for the 128-row tcgen05 tiles
+        self.pair_qblocks = True
         self.last_evidence = None
 
     def budget(self, n_tokens, n_special, n_blocks):
@@ -71,6 +73,9 @@ class SparseGlobalLayer:
                                          dtype=torch.uint8),
                 evidence=torch.empty((s, qbc, cap), device=device, dtype=torch.float32),
             )
+            ws = ops.attention_workspace_size(n_tokens, n_patch, len(slots), self.block,
+                                              self.block) if s else 0
+            buf["attn_ws"] = (torch.empty(ws, device=device, dtype=torch.uint8) if ws else None)
             self._cache[key] = buf
         return buf
 
@@ -99,7 +104,8 @@ class SparseGlobalLayer:
         ops.launch_block_attention(q, kp, vp, ks, vs, buf["indices"], buf["counts"],
                                    buf["slot_ids"], head_dense=buf["dense_flags"],
                                    query_block=self.block, key_block=self.block, out=out,
-                                   evidence=evidence, kernel=self.kernel)
+                                   evidence=evidence, kernel=self.kernel,
+                                   pair_qblocks=self.pair_qblocks, workspace=buf["attn_ws"])
         if events is not None:
             events[2].record()
         self.last_masks = (buf["indices"], buf["counts"])

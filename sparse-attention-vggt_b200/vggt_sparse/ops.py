@@ -42,10 +42,22 @@ def dtype_code(dtype):
     return _DTYPES[dtype]
 
 
+def attention_workspace_size(n_tokens, n_patch, n_slots, query_block=64, key_block=64):
+    """Bytes of the query-block pairing workspace (0 when not paired)."""
+    return int(_lib.load().vggt_block_attention_workspace_size(n_tokens, n_patch, n_slots,
+                                                                 query_block, key_block))
+
+
 def launch_block_attention(q, patch_k, patch_v, special_k, special_v, indices, counts, head_ids,
                            *, head_dense=None, query_block=64, key_block=64, scale=None, out,
-                           evidence=None, status=None, kernel="auto"):
-    """Enqueue one block-sparse attention launch (see vggt_block_attention)."""
+                           evidence=None, status=None, kernel="auto", pair_qblocks=True,
+                           workspace=None):
+    """Enqueue one block-sparse attention launch (see vggt_block_attention).
+
+    With ``pair_qblocks`` (and a kernel choice other than mma_sync) the call
+    goes through vggt_block_attention_ex with a device workspace, so the
+    tcgen05 kernel pairs query blocks by selection overlap; ``workspace`` may
+    pass a reusable uint8 CUDA buffer of at least the size query's bytes."""
     _require_cuda(q, patch_k, patch_v, special_k, special_v, indices, counts, head_ids, head_dense,
                   out, evidence, status)
     _require_contig(q=q, patch_k=patch_k, patch_v=patch_v, special_k=special_k,
@@ -95,11 +107,22 @@ def launch_block_attention(q, patch_k, patch_v, special_k, special_v, indices, c
         raise ValueError("evidence must be float32 with the shape of indices")
     scale = d ** -0.5 if scale is None else float(scale)
     lib = _lib.load()
-    rc = lib.vggt_block_attention(
+    ws_bytes = 0
+    if pair_qblocks and kernel != "mma_sync" and indices.shape[2] > 0:
+        ws_bytes = int(lib.vggt_block_attention_workspace_size(n, npatch, n_slots, query_block,
+                                                               key_block))
+    if ws_bytes > 0:
+        if workspace is None or workspace.numel() < ws_bytes:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+        _require_cuda(workspace)
+    else:
+        workspace = None
+    rc = lib.vggt_block_attention_ex(
         _ptr(q), _ptr(patch_k), _ptr(patch_v), _ptr(special_k), _ptr(special_v), code, h, n,
         npatch, nspecial, d, _ptr(indices), _ptr(counts), per_row, _ptr(head_ids),
         _ptr(head_dense), n_slots, indices.shape[2], query_block, key_block, scale, _ptr(out),
-        _ptr(evidence), _ptr(status), KERNELS[kernel], _stream(q.device))
+        _ptr(evidence), _ptr(status), KERNELS[kernel], _stream(q.device), _ptr(workspace),
+        ws_bytes)
     _lib.check(rc)
     return out, evidence
 

@@ -27,8 +27,9 @@ def lib():
 
 def test_header_declares_the_documented_entry_points():
     assert declared_symbols() == sorted([
-        "vggt_block_attention", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
-        "vggt_block_select", "vggt_sparse_last_error", "vggt_sparse_version"])
+        "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
+        "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc", "vggt_block_select",
+        "vggt_sparse_last_error", "vggt_sparse_version"])
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -36,6 +37,20 @@ def test_library_exports_every_declared_symbol(lib):
     for name in declared_symbols():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, name
+
+
+def test_attention_workspace_size(lib):
+    """Pair table [slots, ceil(QB/2), 2] int32 + bitmaps + window costs +
+    singles, each rounded up to 256 bytes; 0 when the shape is not paired."""
+    up = lambda x: (x + 255) // 256 * 256
+    n, npatch, slots = 43968, 43808, 12
+    qb, nb = -(-n // 64), -(-npatch // 64)
+    nwords = -(-nb // 32)
+    want = (up(slots * -(-qb // 2) * 2 * 4) + up(slots * qb * nwords * 4) +
+            up(slots * qb * 128 * 2) + up(slots * qb * 4))
+    assert lib.vggt_block_attention_workspace_size(n, npatch, slots, 64, 64) == want
+    assert lib.vggt_block_attention_workspace_size(64, npatch, slots, 64, 64) == 0  # one block
+    assert lib.vggt_block_attention_workspace_size(n, npatch, 0, 64, 64) == 0
 
 
 def test_version(lib):
