@@ -90,8 +90,17 @@ __global__ void __launch_bounds__(256) pool_blocks_kernel(const T* __restrict__ 
 // ---------------------------------------------------------------------------
 // Radix select of one row by one warp.
 // ---------------------------------------------------------------------------
+// 4-bit digits, eight passes from the top.  Each lane accumulates the weights
+// (top-k: counts) of its own elements in a private column of the histogram,
+// laid out [digit][lane] so that the 32 lanes hit 32 different 8-byte words:
+// no atomics, no contention even when every key of the row shares its top
+// digits (an fp32 key's top bits are its sign and exponent).
+// Candidate ids are also kept, once they fit, in a per-warp list (uint16) so
+// the remaining passes touch only them.
+constexpr int kCandCap = 512;
 struct SelectHist {
-  unsigned long long w[256];  // per-digit weight (top-k: count) of the candidates
+  unsigned long long w[16][32];
+  uint16_t cand[kCandCap];
 };
 
 __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
@@ -99,12 +108,12 @@ __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
 }
 
 // Selects one row of fp32 scores held in shared memory.  The row is
-// overwritten with the monotone uint32 keys of its scores; for the mass rule
-// wrow receives each block's quantised softmax weight.  Writes ascending
-// selected ids (and -1 padding) to out[0:max_blocks]; returns their count m.
-__device__ int select_row_warp(float* __restrict__ srow, unsigned long long* __restrict__ wrow,
-                               int nb, int mode, int64_t topk, uint64_t tau_num,
-                               SelectHist* hist, int32_t* __restrict__ out,
+// overwritten with the monotone uint32 keys of its scores; mass weights are
+// recomputed from the keys (exactly: a key maps back to its canonical score)
+// for the elements still in the candidate range.  Writes ascending selected
+// ids (and -1 padding) to out[0:max_blocks]; returns their count m.
+__device__ int select_row_warp(float* __restrict__ srow, int nb, int mode, int64_t topk,
+                               uint64_t tau_num, SelectHist* hist, int32_t* __restrict__ out,
                                int64_t max_blocks) {
   const int lane = threadIdx.x & 31;
   const unsigned full = 0xffffffffu;
@@ -118,82 +127,114 @@ __device__ int select_row_warp(float* __restrict__ srow, unsigned long long* __r
 #pragma unroll
     for (int off = 16; off; off >>= 1) rowmax = fmaxf(rowmax, __shfl_xor_sync(full, rowmax, off));
   }
-  // keys (and weights) once per element
-  unsigned long long tw = 0;
+  // keys once per element; the AND and OR of all keys give the leading bits
+  // every key shares
+  uint32_t kand = 0xffffffffu, kor = 0u;
   for (int i = lane; i < nb; i += 32) {
-    const float sc = srow[i];
-    if (mass) {
-      const unsigned long long w = det_mass_weight(sc, rowmax);
-      wrow[i] = w;
-      tw += w;
-    }
-    keys[i] = score_key(sc);
+    const uint32_t key = score_key(srow[i]);
+    keys[i] = key;
+    kand &= key;
+    kor |= key;
   }
-  if (mass) {
-#pragma unroll
-    for (int off = 16; off; off >>= 1) tw += __shfl_xor_sync(full, tw, off);
-    total = tw;
-    target = mass_target(total, tau_num);
-  } else {
-    total = (uint64_t)nb;
-    target = (uint64_t)(topk < (int64_t)nb ? topk : (int64_t)nb);
-  }
+  kand = __reduce_and_sync(full, kand);
+  kor = __reduce_or_sync(full, kor);
+  // top-k: total and target now; mass: the total weight W comes out of the
+  // first radix pass, which sees every element, and then T = ceil(tau W)
+  total = (uint64_t)nb;
+  target = (uint64_t)(topk < (int64_t)nb ? topk : (int64_t)nb);
   __syncwarp();
 
-  int m;
+  int m = -1;
+  uint32_t prefix = 0u, prefix_mask = 0u;
+  unsigned long long above_w = 0;
   // Every block is kept when k >= nb, or when no prefix reaches the mass target
   // (m = #(cum < T) + 1 then exceeds nb and is clamped).  A mass target equal to
   // the total still goes through the radix path: trailing zero-weight blocks
   // are excluded exactly as the reference's cumsum would exclude them.
-  if (target > total || (!mass && target == total)) {
+  if (!mass && target == total) {
     m = nb;
+  } else {
+    // leading bits shared by every key are already decided: start at the
+    // 4-bit digit holding the highest differing bit
+    const uint32_t diff = kand ^ kor;
+    const int top = diff ? 31 - __clz(diff) : 0;
+    const int first = (top / 4) * 4;
+    prefix_mask = first >= 28 ? 0u : (0xffffffffu << (first + 4));
+    prefix = kand & prefix_mask;
+    int ncand = -1;  // length of hist->cand, -1 while the candidates do not fit
+#pragma unroll 1
+    for (int shift = first; shift >= 0; shift -= 4) {
+#pragma unroll
+      for (int d = 0; d < 16; ++d) hist->w[d][lane] = 0ull;
+      const int nscan = ncand < 0 ? nb : ncand;
+      for (int j = lane; j < nscan; j += 32) {
+        const int i = ncand < 0 ? j : (int)hist->cand[j];
+        const uint32_t key = keys[i];
+        if ((key & prefix_mask) == prefix) {
+          const unsigned long long w =
+              mass ? det_mass_weight(__uint_as_float(key_to_bits(key)), rowmax) : 1ull;
+          hist->w[(key >> shift) & 15u][lane] += w;
+        }
+      }
+      __syncwarp();
+      // lane d < 16 totals digit d; the chosen digit is the highest one whose
+      // suffix weight (plus everything already above the prefix) reaches the
+      // target
+      unsigned long long dsum = 0;
+      if (lane < 16) {
+        // skewed columns: the 16 lanes read 16 different banks
+#pragma unroll 8
+        for (int l = 0; l < 32; ++l) dsum += hist->w[lane][(l + lane) & 31];
+      }
+      unsigned long long suffix = dsum;
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) {
+        const unsigned long long v = __shfl_down_sync(full, suffix, off);
+        if (lane + off < 16) suffix += v;
+      }
+      if (mass && shift == first) {
+        // every element is a candidate in the first pass: digit 0's suffix is W
+        total = __shfl_sync(full, suffix, 0);
+        target = mass_target(total, tau_num);
+        if (target > total) {
+          m = nb;
+          break;
+        }
+      }
+      const unsigned ball = __ballot_sync(full, lane < 16 && above_w + suffix >= target);
+      const int digit = 31 - __clz(ball);
+      above_w += __shfl_sync(full, suffix - dsum, digit);
+      prefix |= (uint32_t)digit << shift;
+      prefix_mask |= 15u << shift;
+      __syncwarp();
+      // (re)build the candidate list for the next pass: ids whose key matches
+      // the longer prefix, in id order; abandoned when more than kCandCap match
+      if (shift > 0) {
+        const int nsrc = ncand < 0 ? nb : ncand;
+        int written = 0;
+        for (int base = 0; base < nsrc && written <= kCandCap; base += 32) {
+          const int j = base + lane;
+          int i = 0;
+          bool keep = false;
+          if (j < nsrc) {
+            i = ncand < 0 ? j : (int)hist->cand[j];
+            keep = (keys[i] & prefix_mask) == prefix;
+          }
+          const unsigned kb = __ballot_sync(full, keep);
+          __syncwarp();  // every lane has read its source entry before any write
+          const int pos = written + __popc(kb & lt_mask);
+          if (keep && pos < kCandCap) hist->cand[pos] = (uint16_t)i;
+          written += __popc(kb);
+        }
+        ncand = written <= kCandCap ? written : -1;
+        __syncwarp();
+      }
+    }
+  }
+  if (m == nb) {
     for (int i = lane; i < nb; i += 32)
       if (i < max_blocks) out[i] = i;
   } else {
-    uint32_t prefix = 0, prefix_mask = 0;
-    unsigned long long above_w = 0;
-#pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int bnum = lane; bnum < 256; bnum += 32) hist->w[bnum] = 0ull;
-      __syncwarp();
-      for (int i = lane; i < nb; i += 32) {
-        const uint32_t key = keys[i];
-        if ((key & prefix_mask) == prefix)
-          atomicAdd(&hist->w[(key >> shift) & 255], mass ? wrow[i] : 1ull);
-      }
-      __syncwarp();
-      // lane L owns digits 8L .. 8L+7; find the highest digit whose suffix
-      // weight (plus everything already above the prefix) reaches the target
-      unsigned long long lw[8];
-      unsigned long long lane_w = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        lw[j] = hist->w[8 * lane + j];
-        lane_w += lw[j];
-      }
-      unsigned long long suffix = lane_w;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const unsigned long long v = __shfl_down_sync(full, suffix, off);
-        if (lane + off < 32) suffix += v;
-      }
-      int found = -1;
-      unsigned long long run = above_w + (suffix - lane_w);
-#pragma unroll
-      for (int j = 7; j >= 0; --j) {
-        if (found < 0) {
-          if (run + lw[j] >= target) found = j;
-          else run += lw[j];
-        }
-      }
-      const unsigned ball = __ballot_sync(full, found >= 0);
-      const int win = 31 - __clz(ball);  // highest lane holding a qualifying digit
-      const int digit = __shfl_sync(full, 8 * lane + found, win);
-      above_w = __shfl_sync(full, run, win);
-      prefix |= (uint32_t)digit << shift;
-      prefix_mask |= 255u << shift;
-      __syncwarp();
-    }
     // prefix is now the key of the last selected element; take enough of its
     // ties (lowest ids first) to reach the target
     unsigned long long tie_w = 1ull;
@@ -236,8 +277,7 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
     float* __restrict__ scores_out, const float* __restrict__ scores_in) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SelectHist* hist = reinterpret_cast<SelectHist*>(smem_raw);                // [8]
-  unsigned long long* wrows = reinterpret_cast<unsigned long long*>(hist + 8);  // [RMAX][nb]
-  float* qbar = reinterpret_cast<float*>(wrows + (mode == VGGT_SELECT_MASS ? RMAX * nb : 0));
+  float* qbar = reinterpret_cast<float*>(hist + 8);
   float* srows = qbar + (FROM_SCORES ? 0 : RMAX * D);                       // [RMAX][nb]
 
   const int64_t slot = blockIdx.y;
@@ -274,8 +314,15 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
         }
 #pragma unroll
         for (int r = 0; r < RMAX; ++r) {
+          const float4* q4 = reinterpret_cast<const float4*>(qbar + r * D + i0);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[r] = fmaf(qbar[r * D + i0 + j], kv[j], acc[r]);
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const float4 qv = q4[j4];  // warp-uniform: one broadcast 16-byte read
+            acc[r] = fmaf(qv.x, kv[4 * j4], acc[r]);
+            acc[r] = fmaf(qv.y, kv[4 * j4 + 1], acc[r]);
+            acc[r] = fmaf(qv.z, kv[4 * j4 + 2], acc[r]);
+            acc[r] = fmaf(qv.w, kv[4 * j4 + 3], acc[r]);
+          }
         }
       }
 #pragma unroll
@@ -292,8 +339,8 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
   const int warp = tid >> 5;
   for (int r = warp; r < rows; r += (blockDim.x >> 5)) {
     const int64_t row = slot * qb_count + r0 + r;
-    int m = select_row_warp(srows + (int64_t)r * nb, wrows + (int64_t)r * nb, (int)nb, mode, topk,
-                            tau_num, hist + warp, indices + row * max_blocks, max_blocks);
+    int m = select_row_warp(srows + (int64_t)r * nb, (int)nb, mode, topk, tau_num, hist + warp,
+                            indices + row * max_blocks, max_blocks);
     if ((threadIdx.x & 31) == 0) counts[row] = m;
   }
 }
@@ -302,9 +349,8 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
 // Host launchers
 // ---------------------------------------------------------------------------
 // Shared memory of one selection CTA holding `rows` score rows.
-static size_t select_smem_bytes(int rows, int64_t nb, int d, bool from_scores, bool mass) {
-  return 8 * sizeof(SelectHist) + (size_t)rows * ((from_scores ? 0 : d) + nb) * 4 +
-         (mass ? (size_t)rows * nb * 8 : 0);
+static size_t select_smem_bytes(int rows, int64_t nb, int d, bool from_scores) {
+  return 8 * sizeof(SelectHist) + (size_t)rows * ((from_scores ? 0 : d) + nb) * 4;
 }
 constexpr size_t kSelectSmemBudget = 220 * 1024;
 
@@ -314,7 +360,7 @@ static cudaError_t launch_select_r(const float* pq, const float* pk, int64_t qb_
                                    uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                    int32_t* counts, float* scores_out, const float* scores_in,
                                    cudaStream_t stream) {
-  const size_t smem = select_smem_bytes(RMAX, nb, D, FROM, mode == VGGT_SELECT_MASS);
+  const size_t smem = select_smem_bytes(RMAX, nb, D, FROM);
   auto kern = score_select_kernel<D, FROM, RMAX>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
@@ -333,19 +379,18 @@ static cudaError_t launch_select_t(const float* pq, const float* pk, int64_t qb_
                                    uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                    int32_t* counts, float* scores_out, const float* scores_in,
                                    cudaStream_t stream) {
-  const bool mass = mode == VGGT_SELECT_MASS;
-  if (select_smem_bytes(8, nb, D, FROM, mass) <= kSelectSmemBudget)
+  if (select_smem_bytes(8, nb, D, FROM) <= kSelectSmemBudget)
     return launch_select_r<D, FROM, 8>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
                                        indices, max_blocks, counts, scores_out, scores_in, stream);
-  if (select_smem_bytes(2, nb, D, FROM, mass) <= kSelectSmemBudget)
+  if (select_smem_bytes(2, nb, D, FROM) <= kSelectSmemBudget)
     return launch_select_r<D, FROM, 2>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
                                        indices, max_blocks, counts, scores_out, scores_in, stream);
   return cudaErrorInvalidValue;
 }
 
 int estimator_max_blocks_supported(int d) {
-  // largest nb that still fits two rows per CTA with mass weights
-  return (int)((kSelectSmemBudget - 8 * sizeof(SelectHist)) / (2 * 12) - d);
+  // largest nb that still fits two rows per CTA
+  return (int)((kSelectSmemBudget - 8 * sizeof(SelectHist)) / (2 * 4) - d);
 }
 
 template <typename T>

@@ -178,16 +178,18 @@ def test_select_kernel_bit_exact_with_ties(cuda, mode, budget):
     np.testing.assert_array_equal(ids.cpu().numpy(), exp)
 
 
-def test_select_kernel_bit_exact_random_wide_rows(cuda):
+@pytest.mark.parametrize("rows,width", [(40, 5476), (6, 12000)])
+def test_select_kernel_bit_exact_random_wide_rows(cuda, rows, width):
+    """cfg5-wide rows (8 rows per CTA) and rows past that (2 rows per CTA)."""
     rng = np.random.default_rng(7)
-    scores = (rng.standard_normal((40, 5476)) * 4).astype(np.float32)
+    scores = (rng.standard_normal((rows, width)) * 4).astype(np.float32)
     for mode, b in (("topk", 315), ("mass", 0.85), ("mass", 0.99)):
         ids, counts = vggt_sparse.block_select(torch.tensor(scores, device=cuda), mode=mode,
                                                topk=b if mode == "topk" else None,
                                                tau=b if mode == "mass" else None)
         if mode == "topk":
             exp = oracle.select_topk(scores, b)
-            exp_counts = np.full(40, b)
+            exp_counts = np.full(rows, b)
         else:
             exp, exp_counts = oracle.select_mass(scores, b)
         np.testing.assert_array_equal(counts.cpu().numpy(), exp_counts)
