@@ -112,7 +112,7 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
                             size_t workspace_bytes);
 
 /* Workspace bytes vggt_block_attention_ex needs for query-block pairing (0 when
- * the shape is not paired: fewer than 2 or more than 65536 query blocks or key
+ * the shape is not paired: fewer than 2 query blocks, or more than 65536 key
  * blocks). */
 size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, int64_t n_slots,
                                            int block_q, int block_k);

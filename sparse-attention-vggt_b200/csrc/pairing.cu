@@ -21,7 +21,8 @@
 //      block a takes the unpaired candidate a + d (d <= PAIR_WINDOW) of least
 //      cost (ties -> smallest d); blocks left without a candidate are paired
 //      with each other in order at the end.  Cost rows stream through a
-//      double-buffered shared-memory window.
+//      double-buffered shared-memory window; the taken flags of the
+//      candidate window stay in registers.
 #include <stdint.h>
 
 #include "common.cuh"
@@ -109,23 +110,26 @@ __global__ void __launch_bounds__(COST_THREADS)
 }
 
 // One warp per slot.  pairs [n_slots, ceil(qb_count / 2), 2]; singles is
-// scratch [n_slots, qb_count].  taken [qb_count] flags live in shared memory.
+// scratch [n_slots, qb_count].  Which of the candidates a + 1 .. a + W are
+// already taken lives in registers: lane L holds the bits of d = 4L+1 .. 4L+4,
+// and the window slides by one block per step with one shuffle (a block
+// beyond a + W can only have been taken by a block after a, so zeros shift
+// in).
 __global__ void __launch_bounds__(32)
     greedy_kernel(const uint16_t* __restrict__ cost, const uint8_t* __restrict__ head_dense,
                   int64_t qb_count, int32_t* __restrict__ pairs, int32_t* __restrict__ singles) {
   extern __shared__ unsigned char gsm[];
   uint16_t* rows = reinterpret_cast<uint16_t*>(gsm);  // [2][GREEDY_ROWS][W]
-  unsigned char* taken = gsm + 2 * GREEDY_ROWS * W * sizeof(uint16_t);
   const int lane = threadIdx.x;
+  const unsigned full = 0xffffffffu;
   const int64_t slot = blockIdx.x;
   if (head_dense != nullptr && head_dense[slot]) return;  // the kernel pairs dense slots itself
   const uint16_t* crow = cost + slot * qb_count * W;
   int32_t* out = pairs + slot * ((qb_count + 1) / 2) * 2;
   int32_t* single = singles + slot * qb_count;
-  for (int64_t i = lane; i < qb_count; i += 32) taken[i] = 0;
-  // W / 32 costs per lane per row; the next GREEDY_ROWS rows are fetched into
-  // registers while the current ones are walked, then stored to the other buffer
-  constexpr int PL = W / 32;
+  static_assert(W == 128, "4 candidates per lane");
+  // the next GREEDY_ROWS cost rows are fetched into registers while the
+  // current ones are walked, then stored to the other buffer
   constexpr int NF = GREEDY_ROWS * W / 8 / 32;  // uint4 per lane per buffer
   uint4 pre[NF];
   auto fetch = [&](int64_t r0) {
@@ -145,6 +149,8 @@ __global__ void __launch_bounds__(32)
   fetch(0);
   store(0);
   __syncwarp();
+  uint32_t tk = 0u;        // taken bits of this lane's 4 candidates
+  bool cur_taken = false;  // block a itself
   int64_t np = 0, ns = 0;
   for (int64_t base = 0; base < qb_count; base += GREEDY_ROWS) {
     const int buf = (int)((base / GREEDY_ROWS) & 1);
@@ -153,34 +159,38 @@ __global__ void __launch_bounds__(32)
     const uint16_t* cur = rows + (size_t)buf * GREEDY_ROWS * W;
     const int64_t lim = more ? base + GREEDY_ROWS : qb_count;
     for (int64_t a = base; a < lim; ++a) {
-      __syncwarp();
-      if (taken[a]) continue;  // warp-uniform (shared flag, synced)
-      // best unpaired candidate: key = cost << 16 | d  (ties -> smallest d)
-      uint32_t best = 0xffffffffu;
+      if (!cur_taken) {
+        // this lane's 4 costs: d = 4 lane + 1 .. 4 lane + 4
+        const uint2 c4 = *reinterpret_cast<const uint2*>(cur + (a - base) * W + 4 * lane);
+        const uint32_t cs[4] = {c4.x & 0xffffu, c4.x >> 16, c4.y & 0xffffu, c4.y >> 16};
+        uint32_t best = 0xffffffffu;
 #pragma unroll
-      for (int k = 0; k < PL; ++k) {
-        const int d = lane * PL + k + 1;
-        const int64_t c = a + d;
-        const uint32_t cs = cur[(a - base) * W + d - 1];
-        if (c < qb_count && cs != 0xffffu && !taken[c]) {
-          const uint32_t key = (cs << 16) | (uint32_t)d;
-          best = key < best ? key : best;
+        for (int k = 0; k < 4; ++k) {
+          const int d = 4 * lane + k + 1;
+          if (a + d < qb_count && cs[k] != 0xffffu && !((tk >> k) & 1u)) {
+            const uint32_t key = (cs[k] << 16) | (uint32_t)d;
+            best = key < best ? key : best;
+          }
         }
-      }
-      best = __reduce_min_sync(0xffffffffu, best);
-      __syncwarp();
-      if (lane == 0) {
-        taken[a] = 1;
+        best = __reduce_min_sync(full, best);
         if (best != 0xffffffffu) {
-          const int64_t c = a + (int64_t)(best & 0xffffu);
-          taken[c] = 1;
-          out[2 * np] = (int32_t)a;
-          out[2 * np + 1] = (int32_t)c;
+          const int d = (int)(best & 0xffffu);
+          if (lane == ((d - 1) >> 2)) tk |= 1u << ((d - 1) & 3);
+          if (lane == 0) {
+            out[2 * np] = (int32_t)a;
+            out[2 * np + 1] = (int32_t)(a + d);
+          }
+          ++np;
         } else {
-          single[ns] = (int32_t)a;
+          if (lane == 0) single[ns] = (int32_t)a;
+          ++ns;
         }
       }
-      if (best != 0xffffffffu) ++np; else ++ns;
+      // slide the window to a + 1: block a + 1 (d = 1, lane 0 bit 0) becomes
+      // the current block; lane L's bits take d + 1 from itself and lane L + 1
+      cur_taken = (__shfl_sync(full, tk, 0) & 1u) != 0u;
+      const uint32_t up = __shfl_down_sync(full, tk, 1);
+      tk = (tk >> 1) | ((lane < 31 ? (up & 1u) : 0u) << 3);
     }
     __syncwarp();
     if (more) store(buf ^ 1);
@@ -205,8 +215,8 @@ size_t qblock_pairing_workspace(int64_t n_slots, int64_t qb_count, int64_t nb) {
 }
 
 bool qblock_pairing_supported(int64_t qb_count, int64_t nb) {
-  // greedy flags in shared memory; bitmap kernel: 8 warps' bitmaps in smem
-  return qb_count >= 2 && qb_count <= 65536 && nb >= 1 && nb <= 65536;
+  // bitmap kernel: 8 warps' bitmaps of nb bits in shared memory
+  return qb_count >= 2 && qb_count <= 0x7fffffffLL && nb >= 1 && nb <= 65536;
 }
 
 cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
@@ -238,7 +248,7 @@ cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
                 COST_THREADS, 0, stream>>>(bitmaps, head_dense, qb_count, nwords, cost);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t smem_g = 2 * GREEDY_ROWS * W * sizeof(uint16_t) + (size_t)qb_count;
+  const size_t smem_g = 2 * GREEDY_ROWS * W * sizeof(uint16_t);
   e = cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_g);
   if (e != cudaSuccess) return e;
