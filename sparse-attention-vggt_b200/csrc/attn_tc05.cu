@@ -88,6 +88,7 @@ struct Params {
   int64_t heads, n_tokens, n_patch, n_special, n_slots, max_blocks, qb_count, nb, pairs;
   float* evidence;  // [n_slots, qb_count, max_blocks] or null
   const int32_t* pair_table;  // [indexed slots, pairs, 2] or null
+  const int32_t* work_order;  // [n_slots * pairs] work items in launch order, or null
   int counts_per_qblock;
   float scale_log2;
 };
@@ -189,10 +190,20 @@ __global__ void __launch_bounds__(THREADS, 2)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- work decode: dense-heavy slots (last in the slot order) go first ----
+  // ---- work decode: the given order, else dense-heavy slots (last in the
+  // slot order) first ----
   const int64_t w = blockIdx.x;
-  const int64_t slot = p.n_slots - 1 - w / p.pairs;
-  const int64_t pair = w % p.pairs;
+  int64_t slot = p.n_slots - 1 - w / p.pairs;
+  int64_t pair = w % p.pairs;
+  if (p.work_order != nullptr) {
+    const int64_t item = p.work_order[w];
+    if (item < 0 || item >= p.n_slots * p.pairs) {
+      if (tid == 0 && p.status) atomicOr(p.status, VGGT_STATUS_BAD_INDEX);
+      return;
+    }
+    slot = item / p.pairs;
+    pair = item % p.pairs;
+  }
   const int64_t head = p.head_ids[slot];
   if (head < 0 || head >= p.heads) {
     if (tid == 0 && p.status) atomicOr(p.status, VGGT_STATUS_BAD_HEAD);
@@ -747,6 +758,7 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   p.counts_per_qblock = a.counts_per_qblock;
   p.evidence = a.evidence;
   p.pair_table = a.qblock_pairs;
+  p.work_order = a.work_order;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   const bool evid = a.evidence != nullptr;
   const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4 +

@@ -48,8 +48,10 @@ size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, in
   if (n_tokens <= 0 || n_patch <= 0 || n_slots <= 0 || block_q <= 0 || block_k <= 0) return 0;
   const int64_t qb = cdiv(n_tokens, block_q), nb = cdiv(n_patch, block_k);
   if (!vggt::qblock_pairing_supported(qb, nb)) return 0;
-  return vggt::qblock_pairing_workspace(n_slots, qb, nb) +
-         (((size_t)n_slots * cdiv(qb, 2) * 2 * 4 + 255) & ~(size_t)255);
+  // pair table, work order, then the pairing scratch
+  return (((size_t)n_slots * cdiv(qb, 2) * 2 * 4 + 255) & ~(size_t)255) +
+         (((size_t)n_slots * cdiv(qb, 2) * 4 + 255) & ~(size_t)255) +
+         vggt::qblock_pairing_workspace(n_slots, qb, nb);
 }
 
 int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patch_v,
@@ -115,6 +117,7 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
   a.counts_per_qblock = counts_per_qblock ? 1 : 0;
   a.scale = scale;
   a.qblock_pairs = nullptr;
+  a.work_order = nullptr;
   if (a.qb_count > 0x7fffffffLL) return fail("too many query blocks");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc_ok = vggt::attn_tc05_supported(a);
@@ -127,15 +130,18 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
       if (workspace_bytes < need)
         return fail("workspace of %zu bytes, %zu needed", workspace_bytes, need);
       if (!aligned16(workspace)) return fail("workspace must be 16-byte aligned");
-      // pair table first, then the pairing scratch
-      int32_t* pairs = static_cast<int32_t*>(workspace);
-      void* scratch = static_cast<unsigned char*>(workspace) +
-                      (((size_t)n_slots * cdiv(a.qb_count, 2) * 2 * 4 + 255) & ~(size_t)255);
+      // pair table first, then the work order, then the pairing scratch
+      unsigned char* w = static_cast<unsigned char*>(workspace);
+      int32_t* pairs = reinterpret_cast<int32_t*>(w);
+      w += ((size_t)n_slots * cdiv(a.qb_count, 2) * 2 * 4 + 255) & ~(size_t)255;
+      int32_t* order = reinterpret_cast<int32_t*>(w);
+      w += ((size_t)n_slots * cdiv(a.qb_count, 2) * 4 + 255) & ~(size_t)255;
       const cudaError_t e = vggt::launch_qblock_pairing(indices, counts, a.counts_per_qblock,
                                                         head_dense, n_slots, a.qb_count,
-                                                        max_blocks, a.nb, pairs, scratch, s);
+                                                        max_blocks, a.nb, pairs, order, w, s);
       if (e != cudaSuccess) return cuda_rc(e);
       a.qblock_pairs = pairs;
+      a.work_order = order;
     }
     return cuda_rc(vggt::launch_attn_tc05(a, s));
   }

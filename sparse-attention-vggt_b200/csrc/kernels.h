@@ -38,6 +38,9 @@ struct AttnArgs {
   // [n_indexed_slots, ceil(qb_count / 2), 2] query-block pairs of the
   // indexed slots (second entry -1 when alone), or null for (2p, 2p + 1)
   const int32_t* qblock_pairs;
+  // [n_slots * ceil(qb_count / 2)] work items (slot * pairs + pair) in launch
+  // order, or null for the natural order
+  const int32_t* work_order;
   int64_t heads, n_tokens, n_patch, n_special;
   int64_t n_slots, max_blocks, qb_count, nb;
   int dim, block_q, block_k, dtype, counts_per_qblock;
@@ -51,7 +54,7 @@ bool qblock_pairing_supported(int64_t qb_count, int64_t nb);
 cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
                                   int counts_per_qblock, const uint8_t* head_dense,
                                   int64_t n_slots, int64_t qb_count, int64_t max_blocks,
-                                  int64_t nb, int32_t* pairs, void* workspace,
+                                  int64_t nb, int32_t* pairs, int32_t* order, void* workspace,
                                   cudaStream_t stream);
 
 // attn_mma.cu

@@ -11,7 +11,7 @@
 // row still sees exactly its own key set in ascending block order, so the
 // attention output is bit-identical to the adjacent pairing.
 //
-// Three launches on the caller's stream, all deterministic:
+// Four launches on the caller's stream (the pairs are deterministic):
 //   1. bitmap: one warp per (slot, query block) turns the index list into a
 //      selection bitmap (built in shared memory, stored coalesced).
 //   2. cost:   cost[slot][a][d-1] = popcount(bm[a] ^ bm[a + d]) for the
@@ -22,7 +22,9 @@
 //      cost (ties -> smallest d); blocks left without a candidate are paired
 //      with each other in order at the end.  Cost rows stream through a
 //      double-buffered shared-memory window; the taken flags of the
-//      candidate window stay in registers.
+//      candidate window stay in registers.  Each pair's union size is kept.
+//   4. schedule: the attention grid's work order: slots in the natural order,
+//      each slot's pairs by descending size (the grid ends on short CTAs).
 #include <stdint.h>
 
 #include "common.cuh"
@@ -117,7 +119,9 @@ __global__ void __launch_bounds__(COST_THREADS)
 // in).
 __global__ void __launch_bounds__(32)
     greedy_kernel(const uint16_t* __restrict__ cost, const uint8_t* __restrict__ head_dense,
-                  int64_t qb_count, int32_t* __restrict__ pairs, int32_t* __restrict__ singles) {
+                  const int32_t* __restrict__ counts, int counts_per_qblock, int64_t max_blocks,
+                  int64_t qb_count, int32_t* __restrict__ pairs, int32_t* __restrict__ sizes,
+                  int32_t* __restrict__ singles) {
   extern __shared__ unsigned char gsm[];
   uint16_t* rows = reinterpret_cast<uint16_t*>(gsm);  // [2][GREEDY_ROWS][W]
   const int lane = threadIdx.x;
@@ -126,7 +130,13 @@ __global__ void __launch_bounds__(32)
   if (head_dense != nullptr && head_dense[slot]) return;  // the kernel pairs dense slots itself
   const uint16_t* crow = cost + slot * qb_count * W;
   int32_t* out = pairs + slot * ((qb_count + 1) / 2) * 2;
+  int32_t* osize = sizes + slot * ((qb_count + 1) / 2);
   int32_t* single = singles + slot * qb_count;
+  // selected blocks of query block q (clamped as the attention kernel clamps)
+  auto count_of = [&](int64_t q) -> int32_t {
+    int64_t c = counts_per_qblock ? counts[slot * qb_count + q] : counts[slot];
+    return (int32_t)(c < 0 ? 0 : (c > max_blocks ? max_blocks : c));
+  };
   static_assert(W == 128, "4 candidates per lane");
   // the next GREEDY_ROWS cost rows are fetched into registers while the
   // current ones are walked, then stored to the other buffer
@@ -179,6 +189,8 @@ __global__ void __launch_bounds__(32)
           if (lane == 0) {
             out[2 * np] = (int32_t)a;
             out[2 * np + 1] = (int32_t)(a + d);
+            // tiles of the union: (|A| + |B| + |A xor B|) / 2
+            osize[np] = (count_of(a) + count_of(a + d) + (int32_t)(best >> 16)) / 2;
           }
           ++np;
         } else {
@@ -199,9 +211,53 @@ __global__ void __launch_bounds__(32)
   // leftover blocks pair with each other in order (the last one alone if odd)
   __syncwarp();
   for (int64_t i = lane; 2 * i < ns; i += 32) {
-    out[2 * (np + i)] = single[2 * i];
-    out[2 * (np + i) + 1] = 2 * i + 1 < ns ? single[2 * i + 1] : -1;
+    const int32_t x = single[2 * i];
+    const int32_t y = 2 * i + 1 < ns ? single[2 * i + 1] : -1;
+    out[2 * (np + i)] = x;
+    out[2 * (np + i) + 1] = y;
+    osize[np + i] = count_of(x) + (y >= 0 ? count_of(y) : 0);  // an upper bound
   }
+}
+
+// One CTA per slot: the slots keep the natural launch order (the last slot,
+// where the dense-profiled heads sit, first), so the CTAs in flight share one
+// or two heads' K/V in L2; within a slot the pairs go by descending tile
+// count, so the grid ends on the shortest items.  Sizes fall into
+// SCHED_BUCKETS equal-width buckets of [0, nb]; the order within a bucket is
+// whatever the atomics give (it only changes which CTA runs when).
+constexpr int SCHED_BUCKETS = 1024;
+__global__ void __launch_bounds__(256)
+    schedule_kernel(const int32_t* __restrict__ sizes, const uint8_t* __restrict__ head_dense,
+                    int64_t n_slots, int64_t npairs, int64_t nb, int32_t* __restrict__ order) {
+  __shared__ int hist[SCHED_BUCKETS];
+  const int64_t slot = blockIdx.x;
+  int32_t* dst = order + (n_slots - 1 - slot) * npairs;
+  if (head_dense != nullptr && head_dense[slot]) {  // every pair walks all nb blocks
+    for (int64_t i = threadIdx.x; i < npairs; i += blockDim.x) dst[i] = (int32_t)(slot * npairs + i);
+    return;
+  }
+  for (int i = threadIdx.x; i < SCHED_BUCKETS; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int32_t* sz = sizes + slot * npairs;
+  auto bucket_of = [&](int64_t i) -> int {
+    int64_t v = sz[i];
+    v = v < 0 ? 0 : (v > nb ? nb : v);
+    return (int)((v * (SCHED_BUCKETS - 1)) / (nb > 0 ? nb : 1));
+  };
+  for (int64_t i = threadIdx.x; i < npairs; i += blockDim.x) atomicAdd(&hist[bucket_of(i)], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // exclusive offsets from the largest bucket down
+    int run = 0;
+    for (int b = SCHED_BUCKETS - 1; b >= 0; --b) {
+      const int c = hist[b];
+      hist[b] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < npairs; i += blockDim.x)
+    dst[atomicAdd(&hist[bucket_of(i)], 1)] = (int32_t)(slot * npairs + i);
 }
 
 }  // namespace pairing
@@ -211,7 +267,8 @@ size_t qblock_pairing_workspace(int64_t n_slots, int64_t qb_count, int64_t nb) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
   return up((size_t)n_slots * qb_count * nwords * 4) +        // bitmaps
          up((size_t)n_slots * qb_count * PAIR_WINDOW * 2) +   // costs
-         up((size_t)n_slots * qb_count * 4);                  // singles
+         up((size_t)n_slots * qb_count * 4) +                 // singles
+         up((size_t)n_slots * ((qb_count + 1) / 2) * 4);      // pair sizes
 }
 
 bool qblock_pairing_supported(int64_t qb_count, int64_t nb) {
@@ -220,9 +277,9 @@ bool qblock_pairing_supported(int64_t qb_count, int64_t nb) {
 }
 
 cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
-                                  int counts_per_qblock, const uint8_t* head_dense, int64_t n_slots, int64_t qb_count,
-                                  int64_t max_blocks, int64_t nb, int32_t* pairs, void* workspace,
-                                  cudaStream_t stream) {
+                                  int counts_per_qblock, const uint8_t* head_dense, int64_t n_slots,
+                                  int64_t qb_count, int64_t max_blocks, int64_t nb, int32_t* pairs,
+                                  int32_t* order, void* workspace, cudaStream_t stream) {
   using namespace pairing;
   if (n_slots == 0) return cudaSuccess;
   const int nwords = (int)((nb + 31) / 32);
@@ -233,6 +290,8 @@ cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
   uint16_t* cost = reinterpret_cast<uint16_t*>(ws);
   ws += up((size_t)n_slots * qb_count * W * 2);
   int32_t* singles = reinterpret_cast<int32_t*>(ws);
+  ws += up((size_t)n_slots * qb_count * 4);
+  int32_t* sizes = reinterpret_cast<int32_t*>(ws);
 
   const int64_t rows = n_slots * qb_count;
   const size_t smem_bm = (size_t)BM_WARPS * nwords * 4;
@@ -252,8 +311,12 @@ cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
   e = cudaFuncSetAttribute(greedy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_g);
   if (e != cudaSuccess) return e;
-  greedy_kernel<<<(unsigned)n_slots, 32, smem_g, stream>>>(cost, head_dense, qb_count, pairs,
-                                                           singles);
+  greedy_kernel<<<(unsigned)n_slots, 32, smem_g, stream>>>(
+      cost, head_dense, counts, counts_per_qblock, max_blocks, qb_count, pairs, sizes, singles);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  schedule_kernel<<<(unsigned)n_slots, 256, 0, stream>>>(sizes, head_dense, n_slots,
+                                                        (qb_count + 1) / 2, nb, order);
   return cudaGetLastError();
 }
 

@@ -40,14 +40,16 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_attention_workspace_size(lib):
-    """Pair table [slots, ceil(QB/2), 2] int32 + bitmaps + window costs +
-    singles, each rounded up to 256 bytes; 0 when the shape is not paired."""
+    """Pair table [slots, ceil(QB/2), 2] int32 + work order [slots * ceil(QB/2)]
+    + bitmaps + window costs + singles + pair sizes, each rounded up to 256
+    bytes; 0 when the shape is not paired."""
     up = lambda x: (x + 255) // 256 * 256
     n, npatch, slots = 43968, 43808, 12
     qb, nb = -(-n // 64), -(-npatch // 64)
     nwords = -(-nb // 32)
-    want = (up(slots * -(-qb // 2) * 2 * 4) + up(slots * qb * nwords * 4) +
-            up(slots * qb * 128 * 2) + up(slots * qb * 4))
+    npairs = -(-qb // 2)
+    want = (up(slots * npairs * 2 * 4) + up(slots * npairs * 4) + up(slots * qb * nwords * 4) +
+            up(slots * qb * 128 * 2) + up(slots * qb * 4) + up(slots * npairs * 4))
     assert lib.vggt_block_attention_workspace_size(n, npatch, slots, 64, 64) == want
     assert lib.vggt_block_attention_workspace_size(64, npatch, slots, 64, 64) == 0  # one block
     assert lib.vggt_block_attention_workspace_size(n, npatch, 0, 64, 64) == 0

@@ -134,3 +134,35 @@ def test_layer_uses_pairing_by_default(cuda):
     layer.pair_qblocks = False
     b = layer(x.q, x.kp, x.vp, x.ks, x.vs)
     assert torch.equal(a, b)
+
+
+def test_work_order_is_a_longest_first_permutation(cuda):
+    """The schedule lists every (slot, pair) item once: slots from the last
+    (dense) to the first, each slot's pairs by non-increasing union size."""
+    x, idx, cnt, buf = _layer_masks(cuda, 8, "mass", dense_heads=(0, 5))
+    _, _, ws = _run(x, idx, cnt, buf, pair=True)
+    n_slots = buf["slot_ids"].numel()
+    s_idx, qb, _ = idx.shape
+    npairs = (qb + 1) // 2
+    up = lambda b: (b + 255) // 256 * 256
+    off = up(n_slots * npairs * 2 * 4)
+    order = ws[off: off + n_slots * npairs * 4].view(torch.int32).cpu().numpy()
+    assert sorted(order.tolist()) == list(range(n_slots * npairs))
+    table = ws[: s_idx * npairs * 2 * 4].view(torch.int32).view(s_idx, npairs, 2).cpu().numpy()
+    ids, c = idx.cpu().numpy(), cnt.cpu().numpy()
+    nb = x.shape.n_blocks
+
+    def size(item):
+        slot, p = divmod(int(item), npairs)
+        if slot >= s_idx:
+            return nb
+        a, b = table[slot, p]
+        sa = set(ids[slot, a, :c[slot, a]].tolist())
+        sb = set(ids[slot, b, :c[slot, b]].tolist()) if b >= 0 else set()
+        return len(sa | sb)
+    slots = order // npairs
+    assert np.all(np.diff(slots) <= 0)
+    for slot in range(n_slots):
+        items = order[slots == slot]
+        buckets = np.array([size(i) for i in items]) * 1023 // nb
+        assert np.all(np.diff(buckets) <= 0), slot
