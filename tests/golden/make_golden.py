@@ -16,6 +16,11 @@ Fixtures:
   select_topk.npz     saf3r/patch/adaptive_block_value.py:42-56 select_block_mask
                       (fast path a == count, no history)
   concentration.npz   saf3r/patch/region_history_attention.py:39-42 concentration
+  mask_assembly.npz   saf3r/patch/adaptive_block_value.py:42-91 select_block_mask
+                      with value order, history and every attention/count mix,
+                      plus the same-pass history update of :389-396
+                      (evidence.topk(keep) gathered from the ids); tie-free
+                      inputs (continuous scores, distinct history entries)
   attention_*.npz     the known-answer case of
                       tests/test_adaptive_block_value.py:154-184 (inputs rounded
                       to bf16 so the GPU sees the same values), expected output
@@ -209,7 +214,35 @@ def main(ref_path):
     print("golden fixtures written to", HERE)
 
 
+def mask_assembly(abv):
+    """Fixtures of the full select_block_mask and the history update."""
+    g = torch.Generator().manual_seed(99)
+    rows, blocks, hlen = 24, 150, 20
+    scores = torch.randn(rows, blocks, generator=g) * 2.0
+    value_order = torch.randperm(blocks, generator=g)
+    history = torch.stack([torch.randperm(blocks, generator=g)[:hlen] for _ in range(rows)])
+    history[torch.rand(rows, hlen, generator=g) < 0.2] = -1
+    cases = [(30, 0, False), (30, 30, False), (30, 12, False), (30, 12, True), (30, 30, True),
+             (40, 7, True), (150, 20, True), (30, 1, True)]
+    out = {"scores": scores.numpy(), "value_order": value_order.numpy(),
+           "history": history.numpy(), "cases": np.asarray(cases, dtype=np.int64)}
+    for i, (count, a, use_h) in enumerate(cases):
+        ids, origin = abv.select_block_mask(scores, value_order, count, a,
+                                            history if use_h else None)
+        out["ids_%d" % i] = ids.numpy()
+        out["origin_%d" % i] = origin.numpy()
+    # same-pass history update on case 3 (adaptive_block_value.py:389-396)
+    count, keep = cases[3][0], 10
+    evidence = torch.randn(rows, count, generator=g)
+    winners = evidence.topk(keep, -1).indices
+    out["evidence"] = evidence.numpy()
+    out["keep"] = np.int64(keep)
+    out["new_history"] = torch.as_tensor(out["ids_3"]).gather(1, winners).numpy()
+    np.savez_compressed(os.path.join(HERE, "mask_assembly.npz"), **out)
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: make_golden.py <path to the reference checkout>")
     main(sys.argv[1])
+    mask_assembly(_import_reference(sys.argv[1])[0])
