@@ -47,6 +47,9 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
+    p.add_argument("--component", choices=("layer", "assembly"), default="layer",
+                   help="layer: estimator + attention (the headline); assembly: mask "
+                        "assembly with history and value order + the history update")
     return p.parse_args()
 
 
@@ -307,11 +310,87 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def uniform_value_order(nb):
+    """Bit-reversal coverage order of the key blocks (the uniform branch of
+    saf3r/patch/adaptive_block_value.py:25-38), stable for equal keys."""
+    bits = max(1, math.ceil(math.log2(max(nb, 2))))
+    rev = [int(format(i, "0%db" % bits)[::-1], 2) for i in range(nb)]
+    return sorted(range(nb), key=lambda i: (rev[i], i))
+
+
+def run_assembly_bench(args):
+    """Times vggt_block_mask_assemble (history + value order, every head and
+    query block in one launch) and vggt_history_update on the config's
+    estimator scores; HBM roofline on their algorithmic bytes."""
+    import vggt_sparse
+    from vggt_sparse.configs import CONFIGS
+    from vggt_sparse.synthetic import clustered_layer
+    cfg = CONFIGS[args.config]
+    device = torch.device("cuda", torch.cuda.current_device())
+    x = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device=device, keep_full=False)
+    sparse = [h for h in range(16) if h not in cfg.dense_heads]
+    nb = x.shape.n_blocks
+    budget = vggt_sparse.topk_budget(cfg.retention if cfg.mode == "topk" else 0.25,
+                                     x.shape.n_tokens, x.shape.n_special, nb, cfg.block)
+    res = vggt_sparse.block_mask_estimate(x.q, x.kp, head_ids=torch.tensor(sparse, device=device,
+                                                                            dtype=torch.int32),
+                                          query_block=cfg.block, key_block=cfg.block, mode="topk",
+                                          topk=budget, export_scores=True)
+    scores = res.scores.contiguous()
+    s, qb, _ = scores.shape
+    del x, res
+    order = uniform_value_order(nb)
+    counts, acnt = [budget] * s, [budget // 2] * s
+    keep = max(1, budget // 2)
+    ids, _ = vggt_sparse.assemble_masks(scores, order, counts, acnt)
+    ev = torch.randn(ids.shape, device=device)
+    hist = vggt_sparse.history_update(ev, ids, counts, [keep] * s)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device)
+
+    def step():
+        i2, _ = vggt_sparse.assemble_masks(scores, order, counts, acnt, hist, max_blocks=budget)
+        vggt_sparse.history_update(ev, i2, counts, [keep] * s, history_len=keep)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    rows = s * qb
+    nbytes = rows * (nb * 4 + keep * 4 + budget * 5) + rows * (budget * 8 + keep * 4)
+    peaks = load_peaks()
+    line = {"metric": "ms per mask assembly (history + value order) + history update, all heads",
+            "value": ms, "unit": "ms", "component": "assembly", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "%s estimator scores: %d heads x %d query blocks x %d key "
+                                   "blocks, count %d, attention %d, history %d"
+                                   % (cfg.name, s, qb, nb, budget, budget // 2, keep),
+                       "l2": "256 MB flush between steps"},
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                         "bytes_per_step": nbytes},
+            "gpu_launches": 2 * args.steps}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.component == "assembly":
+        if rank == 0:
+            run_assembly_bench(args)
         return
     import vggt_sparse
     from vggt_sparse import ops

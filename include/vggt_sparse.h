@@ -118,6 +118,50 @@ size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, in
                                            int block_q, int block_k);
 
 /*
+ * Mask assembly with history and value order.  Replaces
+ * saf3r/patch/adaptive_block_value.py:42-91 (select_block_mask), run there per
+ * head in Python, for every (slot, query block) row in one launch.
+ *
+ * scores            [n_slots, n_qblocks, n_blocks] fp32 relevance per key block
+ * value_order       [n_blocks] int32, the value-coverage order of the blocks
+ * counts            [n_slots] int32, blocks per row (the reference's `count`)
+ * attention_counts  [n_slots] int32, attention-chosen blocks (`attention_count`)
+ * history           [n_slots, n_qblocks, history_len] int32 block ids of the
+ *                   previous layer, -1 where empty; NULL (or history_len 0) = none
+ * ids               out [n_slots, n_qblocks, max_blocks] int32: ascending ids,
+ *                   -1 padded
+ * origin            out [n_slots, n_qblocks, max_blocks] uint8 or NULL:
+ *                   1 reused from history, 2 attention, 0 value fill
+ * With history and attention_count >= 2, up to attention_count / 2 history
+ * blocks are reused when their current score ranks within the top
+ * 2 * attention_count; the rest of the attention slots take the best current
+ * scores; count - attention_count slots take uncovered blocks in value order.
+ * Ties rank the lower block id (or history position) first; the reference's
+ * torch.topk leaves their order unspecified.  n_blocks up to about 50,000.
+ */
+int vggt_block_mask_assemble(const float* scores, int64_t n_slots, int64_t n_qblocks,
+                             int64_t n_blocks, const int32_t* value_order, const int32_t* counts,
+                             const int32_t* attention_counts, const int32_t* history,
+                             int64_t history_len, int32_t* ids, uint8_t* origin,
+                             int64_t max_blocks, int32_t* status, void* stream);
+
+/*
+ * Same-pass history update.  Replaces adaptive_block_value.py:389-396
+ * (winners = evidence.topk(keep); new_history = masks.gather(winners)).
+ *
+ * evidence     [n_slots, n_qblocks, max_blocks] fp32 (vggt_block_attention)
+ * ids          [n_slots, n_qblocks, max_blocks] int32 ascending mask ids
+ * counts/keeps [n_slots] int32: slots in use per row, history blocks to keep
+ * new_history  out [n_slots, n_qblocks, history_len] int32: the keep ids of
+ *              largest evidence (ties to the lower slot), ascending, -1 padded
+ *              (the reference keeps evidence order; later layers use the set)
+ */
+int vggt_history_update(const float* evidence, const int32_t* ids, int64_t n_slots,
+                        int64_t n_qblocks, int64_t max_blocks, const int32_t* counts,
+                        const int32_t* keeps, int32_t* new_history, int64_t history_len,
+                        void* stream);
+
+/*
  * Block-mask estimator.  Mean-pools q over query blocks of block_q tokens and
  * patch_k over key blocks of block_k tokens (saf3r/patch/adaptive_block_value.py:16-23,
  * applied to both), forms pooled scores S = (Qbar . Kbar^T) * scale in fp32

@@ -162,6 +162,47 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
                                  nullptr, 0);
 }
 
+int vggt_block_mask_assemble(const float* scores, int64_t n_slots, int64_t n_qblocks,
+                             int64_t n_blocks, const int32_t* value_order, const int32_t* counts,
+                             const int32_t* attention_counts, const int32_t* history,
+                             int64_t history_len, int32_t* ids, uint8_t* origin,
+                             int64_t max_blocks, int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (n_slots < 0 || n_qblocks < 0 || n_blocks < 0 || history_len < 0 || max_blocks < 0)
+    return fail("negative size argument");
+  if (n_slots > 65535) return fail("n_slots %lld exceeds 65535", (long long)n_slots);
+  if (n_slots == 0 || n_qblocks == 0) return 0;
+  if (n_blocks < 1) return fail("n_blocks must be >= 1");
+  if (history_len > 0x7fffffffLL) return fail("history_len too large");
+  if (!vggt::assemble_supported(n_blocks))
+    return fail("n_blocks %lld exceeds what one row's shared memory holds (about 50,000)",
+                (long long)n_blocks);
+  if (max_blocks < 1) return fail("max_blocks must be >= 1");
+  if (!scores || !value_order || !counts || !attention_counts || !ids)
+    return fail("scores, value_order, counts, attention_counts and ids must be non-NULL");
+  if (history_len > 0 && !history) return fail("history must be non-NULL when history_len > 0");
+  return cuda_rc(vggt::launch_assemble(scores, n_slots, n_qblocks, n_blocks, value_order, counts,
+                                       attention_counts, history_len > 0 ? history : nullptr,
+                                       history_len, ids, origin, max_blocks, status,
+                                       static_cast<cudaStream_t>(stream)));
+}
+
+int vggt_history_update(const float* evidence, const int32_t* ids, int64_t n_slots,
+                        int64_t n_qblocks, int64_t max_blocks, const int32_t* counts,
+                        const int32_t* keeps, int32_t* new_history, int64_t history_len,
+                        void* stream) {
+  g_err[0] = '\0';
+  if (n_slots < 0 || n_qblocks < 0 || max_blocks < 0 || history_len < 0)
+    return fail("negative size argument");
+  if (n_slots == 0 || n_qblocks == 0 || history_len == 0) return 0;
+  if (max_blocks > 0x7fffffffLL) return fail("max_blocks too large");
+  if (!evidence || !ids || !counts || !keeps || !new_history)
+    return fail("evidence, ids, counts, keeps and new_history must be non-NULL");
+  return cuda_rc(vggt::launch_history_update(evidence, ids, n_slots, n_qblocks, max_blocks, counts,
+                                             keeps, new_history, history_len,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
 int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int64_t heads,
                              int64_t n_tokens, int64_t n_patch, int dim, const int32_t* head_ids,
                              int64_t n_slots, int block_q, int block_k, int mode, int64_t topk,

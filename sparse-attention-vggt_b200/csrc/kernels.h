@@ -57,6 +57,20 @@ cudaError_t launch_qblock_pairing(const int32_t* indices, const int32_t* counts,
                                   int64_t nb, int32_t* pairs, int32_t* order, void* workspace,
                                   cudaStream_t stream);
 
+// assembly.cu: select_block_mask with history and value order; history update
+constexpr size_t kAssembleSmemBudget = 220 * 1024;
+size_t assemble_smem_per_row(int64_t nb);
+bool assemble_supported(int64_t nb);
+cudaError_t launch_assemble(const float* scores, int64_t n_slots, int64_t qb_count, int64_t nb,
+                            const int32_t* value_order, const int32_t* counts,
+                            const int32_t* attention_counts, const int32_t* history,
+                            int64_t hlen, int32_t* ids, uint8_t* origin, int64_t max_blocks,
+                            int32_t* status, cudaStream_t stream);
+cudaError_t launch_history_update(const float* evidence, const int32_t* ids, int64_t n_slots,
+                                  int64_t qb_count, int64_t max_blocks, const int32_t* counts,
+                                  const int32_t* keeps, int32_t* out, int64_t out_len,
+                                  cudaStream_t stream);
+
 // attn_mma.cu
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu

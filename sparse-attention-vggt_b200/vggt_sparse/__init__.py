@@ -8,6 +8,7 @@ dispatch and multi-GPU sharding.  All compute runs in ``libvggt_sparse.so``
 """
 from . import ops  # noqa: F401  (registers torch.ops.vggt_sparse.*)
 from ._lib import ExtensionMissing, load as load_library  # noqa: F401
+from .assembly import assemble_masks, history_update, select_block_mask  # noqa: F401
 from .block_attention import block_attention  # noqa: F401
 from .configs import CONFIGS, LayerConfig  # noqa: F401
 from .estimator import BlockMasks, block_mask_estimate, block_select  # noqa: F401

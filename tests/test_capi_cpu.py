@@ -28,8 +28,9 @@ def lib():
 def test_header_declares_the_documented_entry_points():
     assert declared_symbols() == sorted([
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
-        "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc", "vggt_block_select",
-        "vggt_sparse_last_error", "vggt_sparse_version"])
+        "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
+        "vggt_block_select", "vggt_history_update", "vggt_sparse_last_error",
+        "vggt_sparse_version"])
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -116,6 +117,24 @@ def test_estimator_argument_errors(lib, bad, msg):
     rc = _est(lib, **bad)
     assert rc < 0
     assert msg in lib.vggt_sparse_last_error().decode()
+
+
+def test_assemble_and_history_argument_errors(lib):
+    asm = lambda **kw: lib.vggt_block_mask_assemble(*dict(dict(
+        scores=16, s=1, qb=4, nb=100, vo=16, counts=16, a=16, hist=None, hlen=0, ids=16, org=None,
+        maxk=8, status=None, stream=None), **kw).values())
+    assert asm(s=-1) < 0
+    assert asm(nb=0) < 0 and "n_blocks" in lib.vggt_sparse_last_error().decode()
+    assert asm(nb=100000) < 0 and "exceeds" in lib.vggt_sparse_last_error().decode()
+    assert asm(scores=None) < 0 and "non-NULL" in lib.vggt_sparse_last_error().decode()
+    assert asm(hlen=5) < 0 and "history" in lib.vggt_sparse_last_error().decode()
+    assert asm(maxk=0) < 0
+    assert asm(s=0) == 0
+    hist = lambda **kw: lib.vggt_history_update(*dict(dict(
+        ev=16, ids=16, s=1, qb=4, maxk=8, counts=16, keeps=16, out=16, hlen=4, stream=None),
+        **kw).values())
+    assert hist(ev=None) < 0
+    assert hist(hlen=0) == 0
 
 
 def test_select_argument_errors(lib):
