@@ -47,9 +47,11 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
-    p.add_argument("--component", choices=("layer", "assembly"), default="layer",
+    p.add_argument("--component", choices=("layer", "assembly", "triton-ref"), default="layer",
                    help="layer: estimator + attention (the headline); assembly: mask "
-                        "assembly with history and value order + the history update")
+                        "assembly with history and value order + the history update; "
+                        "triton-ref: the reference's own Triton block_attention (installed "
+                        "in baseline/_ref) against this drop-in on the same inputs and masks")
     return p.parse_args()
 
 
@@ -382,6 +384,70 @@ def run_assembly_bench(args):
     print(json.dumps(line), flush=True)
 
 
+def run_triton_reference_comparison(args):
+    """The reference's Triton block_attention (saf3r/triton/adaptive_block_attention.py,
+    installed into baseline/_ref) and vggt_sparse.block_attention on the same
+    top-k masks (one count per head, as the reference kernel reads it), all 16
+    heads sparse, evidence on for both.  Prints one JSON line per shape."""
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    try:
+        sys.path.insert(0, ref_dir)
+        from saf3r.triton.adaptive_block_attention import block_attention as ref_ba
+    except Exception as e:  # not installed on this machine
+        print(json.dumps({"component": "triton-ref",
+                          "unavailable": "reference not importable from baseline/_ref: %r" % e}))
+        return
+    import vggt_sparse
+    from vggt_sparse.synthetic import clustered_layer
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+
+    def timeit(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+    for frames, centres, rho in [(4, 64, 0.25), (32, 128, 0.25), (100, 256, 0.15)]:
+        x = clustered_layer(frames, centres=centres, seed=0, device=dev)
+        layer = vggt_sparse.SparseGlobalLayer(16, mode="topk", retention=rho, kernel="tcgen05")
+        layer.topk = vggt_sparse.topk_budget(rho, x.shape.n_tokens, x.shape.n_special,
+                                             x.shape.n_blocks, 64)
+        layer(x.q, x.kp, x.vp, x.ks, x.vs)
+        idx, cnt = layer.last_masks
+        flops = layer.kept_flops(x.shape.n_tokens, x.shape.n_patch, x.shape.n_special, 64)
+        counts = cnt[:, 0].contiguous()
+        heads = torch.arange(16, device=dev, dtype=torch.int32)
+        args_ = (x.q, x.kp, x.vp, x.ks, x.vs, idx, counts, heads)
+        o_ref, ev_ref = ref_ba(*args_)
+        o_us, ev_us = vggt_sparse.block_attention(*args_)
+        torch.cuda.synchronize()
+        fin = torch.isfinite(ev_ref)
+        t_ref = timeit(lambda: ref_ba(*args_))
+        t_us = timeit(lambda: vggt_sparse.block_attention(*args_, validate=False))
+        t_noev = timeit(lambda: vggt_sparse.block_attention(*args_, validate=False,
+                                                            return_evidence=False))
+        print(json.dumps({
+            "component": "triton-ref", "unit": "ms",
+            "workload": "%d frames (%d tokens), 16 sparse heads x 64, top-k %.2f (%d blocks)"
+                        % (frames, x.shape.n_tokens, rho, layer.topk),
+            "reference_triton_ms": t_ref, "ours_ms": t_us, "ours_no_evidence_ms": t_noev,
+            "speedup": t_ref / t_us, "kept_tflop": flops / 1e12,
+            "reference_tflops": flops / t_ref / 1e9, "ours_tflops": flops / t_us / 1e9,
+            "max_abs_out_diff": (o_ref.float() - o_us.float()).abs().max().item(),
+            "max_abs_evidence_diff": (ev_ref[fin] - ev_us[fin]).abs().max().item(),
+            "same_empty_slots": bool(torch.equal(fin, torch.isfinite(ev_us))),
+            "steps": args.steps, "warmup": args.warmup}), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
@@ -391,6 +457,10 @@ def main():
     if args.component == "assembly":
         if rank == 0:
             run_assembly_bench(args)
+        return
+    if args.component == "triton-ref":
+        if rank == 0:
+            run_triton_reference_comparison(args)
         return
     import vggt_sparse
     from vggt_sparse import ops
