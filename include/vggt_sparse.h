@@ -97,7 +97,12 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
  * memory), it first pairs the query blocks of every indexed slot so that the
  * two selections of a tile differ least (three small kernels on `stream`),
  * which removes most of the masked tile work; the output is bit-identical
- * to the unpaired run.  workspace == NULL, or a kernel choice other than
+ * to the unpaired run.  When the grid is small (fewer than ~2,400 128-row
+ * work items, e.g. one rank's query-block shard), the workspace also holds
+ * partial results: each work item's key tiles are split over 2-4 CTAs and a
+ * second launch merges them (output within rounding of the unsplit run; the
+ * environment variable VGGT_ATTN_SPLIT=1..4 fixes the split, for both this
+ * call and the size query).  workspace == NULL, or a kernel choice other than
  * tcgen05, runs exactly vggt_block_attention.  A workspace smaller than the
  * size query is an argument error.
  */

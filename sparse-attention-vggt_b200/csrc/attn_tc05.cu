@@ -89,6 +89,14 @@ struct Params {
   float* evidence;  // [n_slots, qb_count, max_blocks] or null
   const int32_t* pair_table;  // [indexed slots, pairs, 2] or null
   const int32_t* work_order;  // [n_slots * pairs] work items in launch order, or null
+  // Split of each work item's tile list over nsplit CTAs (1 = none).  With
+  // nsplit > 1 a CTA writes its unnormalised O, row sum and reference max to
+  // `partial` ([item][split][66][128] fp32) and split 0 the destination row of
+  // each of its 128 rows to `part_rows` ([item][128], -1 = none); the combine
+  // kernel then writes `out`.
+  int nsplit;
+  float* partial;
+  int64_t* part_rows;
   int counts_per_qblock;
   float scale_log2;
 };
@@ -191,8 +199,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // ---- work decode: the given order, else dense-heavy slots (last in the
-  // slot order) first ----
-  const int64_t w = blockIdx.x;
+  // slot order) first; consecutive CTAs take the splits of one item ----
+  const int64_t w = blockIdx.x / p.nsplit;
+  const int split = (int)(blockIdx.x % p.nsplit);
   int64_t slot = p.n_slots - 1 - w / p.pairs;
   int64_t pair = w % p.pairs;
   if (p.work_order != nullptr) {
@@ -276,7 +285,11 @@ __global__ void __launch_bounds__(THREADS, 2)
     n_patch_tiles = misc[2];
   }
   const int64_t n_spec_tiles = (p.n_special + BN - 1) / BN;
-  const int64_t n_tiles = n_patch_tiles + n_spec_tiles;
+  // this CTA's share [t0, t0 + n_tiles) of the item's tiles (patch tiles in
+  // ascending order, then the special tiles)
+  const int64_t n_all = n_patch_tiles + n_spec_tiles;
+  const int64_t t0 = n_all * split / p.nsplit;
+  const int64_t n_tiles = n_all * (split + 1) / p.nsplit - t0;
 
   // ---- barriers and TMEM ----
   if (tid == 0) {
@@ -327,9 +340,28 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (!dense && nwords > 0) {
         curA = bmA[0];
         cur = curA | bmB[0];
+        // skip the union's first t0 blocks (earlier splits' tiles)
+        int64_t skip = t0 < n_patch_tiles ? t0 : n_patch_tiles;
+        while (skip > 0) {
+          const int c = __popc(cur);
+          if (c <= skip) {
+            skip -= c;
+            ++wi;
+            if (wi < nwords) {
+              curA = bmA[wi];
+              cur = curA | bmB[wi];
+            } else {
+              cur = 0u;
+            }
+          } else {
+            for (int64_t k = 0; k < skip; ++k) cur &= cur - 1u;
+            skip = 0;
+          }
+        }
       }
       int64_t issued = 0;
       for (int64_t t = 0; t < n_tiles; ++t) {
+        const int64_t g = t0 + t;  // index in the item's tile list
         const int stage = (int)(t % NSTAGE);
         if (t >= NSTAGE) {
           if (!tc::mbar_wait(bar(B_KVEMPTY + stage), (uint32_t)((t / NSTAGE - 1) & 1), abort_flag,
@@ -338,10 +370,10 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         int flags, ncols, row;
         const CUtensorMap *mk, *mv;
-        if (t < n_patch_tiles) {
+        if (g < n_patch_tiles) {
           int64_t kb;
           if (dense) {
-            kb = t;
+            kb = g;
             flags = 3;
           } else {
             while (cur == 0u) {
@@ -359,7 +391,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           mk = &tm_kp;
           mv = &tm_vp;
         } else {
-          const int64_t st = t - n_patch_tiles;
+          const int64_t st = g - n_patch_tiles;
           flags = 3;
           row = (int)(st * BN);
           ncols = (int)(p.n_special - st * BN < BN ? p.n_special - st * BN : BN);
@@ -367,7 +399,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           mv = &tm_vs;
         }
         if (t == n_tiles - 1) flags |= 4;
-        const bool special = t >= n_patch_tiles;
+        const bool special = g >= n_patch_tiles;
         // bits 0-1 query-block flags, 2 last, 3 special, 4-10 valid columns,
         // 12-31 patch block id
         meta[stage] = flags | (special ? 8 : 0) | (ncols << 4) |
@@ -627,6 +659,27 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tmem_wait_ld();
       l = __uint_as_float(r[0]);
     }
+    if (p.nsplit > 1) {
+      // partial result: O and l relative to 2^(m_ref * c), coalesced by row
+      float* part = p.partial + ((w * p.nsplit + split) * 66) * 128;
+      const bool have = ok && n_tiles > 0;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t r[32];
+        if (have) {
+          tc::tmem_ld32(t_o + lane_off + 32u * h2, r);
+          tc::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) part[(h2 * 32 + i) * 128 + row] = __uint_as_float(r[i]);
+      }
+      part[64 * 128 + row] = have ? l : 0.f;
+      part[65 * 128 + row] = (have && has_mass) ? m_ref * c : -INFINITY;
+      if (split == 0) p.part_rows[w * 128 + row] = valid_row ? head * p.n_tokens + qrow : -1;
+    } else {
     const float inv = l > 0.f ? 1.f / l : 0.f;
     T* dst = static_cast<T*>(p.out) + (head * p.n_tokens + qrow) * HD;
 #pragma unroll
@@ -655,6 +708,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
       }
     }
+    }
   }
 
   tc::tc_fence_before();
@@ -669,6 +723,47 @@ __global__ void __launch_bounds__(THREADS, 2)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+// Merges the nsplit partial results of each work item (one CTA per item, one
+// thread per row): with M the largest reference max over the splits,
+// out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+template <typename T>
+__global__ void __launch_bounds__(128)
+    combine_splits_kernel(const float* __restrict__ partial, const int64_t* __restrict__ part_rows,
+                          int nsplit, T* __restrict__ out) {
+  const int64_t item = blockIdx.x;
+  const int row = threadIdx.x;
+  const int64_t dst = part_rows[item * 128 + row];
+  if (dst < 0) return;
+  const float* base = partial + item * nsplit * 66 * 128;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, base[(s * 66 + 65) * 128 + row]);
+  float acc[64];
+#pragma unroll
+  for (int d = 0; d < 64; ++d) acc[d] = 0.f;
+  float l = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = base[(s * 66 + 65) * 128 + row];
+      if (ms == -INFINITY) continue;
+      const float wgt = exp2f(ms - mx);
+      l = fmaf(wgt, base[(s * 66 + 64) * 128 + row], l);
+#pragma unroll
+      for (int d = 0; d < 64; ++d) acc[d] = fmaf(wgt, base[(s * 66 + d) * 128 + row], acc[d]);
+    }
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  uint4* o = reinterpret_cast<uint4*>(out + dst * HD);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint4 v;
+    v.x = ElemOps<T>::pack2(acc[8 * q + 0] * inv, acc[8 * q + 1] * inv);
+    v.y = ElemOps<T>::pack2(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
+    v.z = ElemOps<T>::pack2(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
+    v.w = ElemOps<T>::pack2(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
+    o[q] = v;
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -759,11 +854,15 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   p.evidence = a.evidence;
   p.pair_table = a.qblock_pairs;
   p.work_order = a.work_order;
+  p.nsplit = a.nsplit > 1 && a.partial != nullptr && a.part_rows != nullptr ? a.nsplit : 1;
+  p.partial = a.partial;
+  p.part_rows = a.part_rows;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   const bool evid = a.evidence != nullptr;
   const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4 +
                       (evid ? 2 * (size_t)((a.nb + 7) & ~7LL) * 2 : 0);
-  const int64_t grid = a.n_slots * p.pairs;
+  const int64_t items = a.n_slots * p.pairs;
+  const int64_t grid = items * p.nsplit;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   cudaError_t e;
   if (a.dtype == VGGT_DTYPE_BF16)
@@ -773,7 +872,29 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
     e = evid ? launch_kernel<__half, true>(grid, smem, stream, mkp, mvp, mks, mvs, p)
              : launch_kernel<__half, false>(grid, smem, stream, mkp, mvp, mks, mvs, p);
   if (e != cudaSuccess) return e;
+  if (p.nsplit > 1) {
+    if (a.dtype == VGGT_DTYPE_BF16)
+      combine_splits_kernel<__nv_bfloat16><<<(unsigned)items, 128, 0, stream>>>(
+          p.partial, p.part_rows, p.nsplit, static_cast<__nv_bfloat16*>(a.out));
+    else
+      combine_splits_kernel<__half><<<(unsigned)items, 128, 0, stream>>>(
+          p.partial, p.part_rows, p.nsplit, static_cast<__half*>(a.out));
+  }
   return cudaGetLastError();
+}
+
+int64_t attn_tc05_split(int64_t items) {
+  // enough CTAs for about 8 waves of 2 CTAs on 148 SMs, at most 4 splits
+  constexpr int64_t kTargetCtas = 8 * 2 * 148;
+  if (items <= 0 || items >= kTargetCtas) return 1;
+  const int64_t s = (kTargetCtas + items - 1) / items;
+  return s > 4 ? 4 : s;
+}
+
+size_t attn_tc05_split_bytes(int64_t items, int64_t nsplit) {
+  if (nsplit <= 1) return 0;
+  return (((size_t)items * nsplit * 66 * 128 * 4 + 255) & ~(size_t)255) +
+         (((size_t)items * 128 * 8 + 255) & ~(size_t)255);
 }
 
 }  // namespace vggt

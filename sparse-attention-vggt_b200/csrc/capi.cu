@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -35,6 +36,16 @@ int cuda_rc(cudaError_t e) {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Splits per work item of the tcgen05 kernel: VGGT_ATTN_SPLIT (1-4) when set,
+// else enough for about 8 waves of CTAs (1 for large grids).
+int64_t attention_split(int64_t items) {
+  if (const char* env = std::getenv("VGGT_ATTN_SPLIT")) {
+    const long v = std::strtol(env, nullptr, 10);
+    if (v >= 1 && v <= 4) return v;
+  }
+  return vggt::attn_tc05_split(items);
+}
+
 }  // namespace
 
 extern "C" {
@@ -48,10 +59,12 @@ size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, in
   if (n_tokens <= 0 || n_patch <= 0 || n_slots <= 0 || block_q <= 0 || block_k <= 0) return 0;
   const int64_t qb = cdiv(n_tokens, block_q), nb = cdiv(n_patch, block_k);
   if (!vggt::qblock_pairing_supported(qb, nb)) return 0;
-  // pair table, work order, then the pairing scratch
+  // pair table, work order, the pairing scratch, then the split partials
+  const int64_t items = n_slots * cdiv(qb, 2);
   return (((size_t)n_slots * cdiv(qb, 2) * 2 * 4 + 255) & ~(size_t)255) +
          (((size_t)n_slots * cdiv(qb, 2) * 4 + 255) & ~(size_t)255) +
-         vggt::qblock_pairing_workspace(n_slots, qb, nb);
+         vggt::qblock_pairing_workspace(n_slots, qb, nb) +
+         vggt::attn_tc05_split_bytes(items, attention_split(items));
 }
 
 int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patch_v,
@@ -118,6 +131,9 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
   a.scale = scale;
   a.qblock_pairs = nullptr;
   a.work_order = nullptr;
+  a.nsplit = 1;
+  a.partial = nullptr;
+  a.part_rows = nullptr;
   if (a.qb_count > 0x7fffffffLL) return fail("too many query blocks");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc_ok = vggt::attn_tc05_supported(a);
@@ -142,6 +158,16 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
       if (e != cudaSuccess) return cuda_rc(e);
       a.qblock_pairs = pairs;
       a.work_order = order;
+      // split partials after the pairing scratch
+      const int64_t items = n_slots * cdiv(a.qb_count, 2);
+      const int64_t nsplit = attention_split(items);
+      if (nsplit > 1) {
+        unsigned char* sp = w + vggt::qblock_pairing_workspace(n_slots, a.qb_count, a.nb);
+        a.nsplit = (int)nsplit;
+        a.partial = reinterpret_cast<float*>(sp);
+        a.part_rows = reinterpret_cast<int64_t*>(
+            sp + (((size_t)items * nsplit * 66 * 128 * 4 + 255) & ~(size_t)255));
+      }
     }
     return cuda_rc(vggt::launch_attn_tc05(a, s));
   }

@@ -41,6 +41,11 @@ struct AttnArgs {
   // [n_slots * ceil(qb_count / 2)] work items (slot * pairs + pair) in launch
   // order, or null for the natural order
   const int32_t* work_order;
+  // tcgen05 only: each work item's tiles split over nsplit CTAs, merged by a
+  // second launch; partial / part_rows sized by attn_tc05_split_bytes
+  int nsplit;
+  float* partial;
+  int64_t* part_rows;
   int64_t heads, n_tokens, n_patch, n_special;
   int64_t n_slots, max_blocks, qb_count, nb;
   int dim, block_q, block_k, dtype, counts_per_qblock;
@@ -76,5 +81,9 @@ cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu
 bool attn_tc05_supported(const AttnArgs& a);
 cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream);
+// splits per work item for a grid of `items` 128-row work items, and the
+// scratch bytes the split needs (0 when nsplit <= 1)
+int64_t attn_tc05_split(int64_t items);
+size_t attn_tc05_split_bytes(int64_t items, int64_t nsplit);
 
 }  // namespace vggt

@@ -97,7 +97,8 @@ def test_pair_table_matches_restatement_and_covers_every_block(cuda, mode):
 
 @pytest.mark.parametrize("mode", ["topk", "mass"])
 @pytest.mark.parametrize("evidence", [False, True])
-def test_pairing_leaves_outputs_bit_identical(cuda, mode, evidence):
+def test_pairing_leaves_outputs_bit_identical(cuda, mode, evidence, monkeypatch):
+    monkeypatch.setenv("VGGT_ATTN_SPLIT", "1")  # no key-range split: same summation order
     x, idx, cnt, buf = _layer_masks(cuda, 8, mode, dense_heads=(0, 5))
     out0, ev0, _ = _run(x, idx, cnt, buf, pair=False, evidence=evidence)
     out1, ev1, _ = _run(x, idx, cnt, buf, pair=True, evidence=evidence)
@@ -125,7 +126,8 @@ def test_pairing_reduces_union_tiles(cuda):
     assert union_tiles(table) < union_tiles(adjacent)
 
 
-def test_layer_uses_pairing_by_default(cuda):
+def test_layer_uses_pairing_by_default(cuda, monkeypatch):
+    monkeypatch.setenv("VGGT_ATTN_SPLIT", "1")
     x = clustered_layer(4, centres=64, seed=1, device=cuda)
     layer = vggt_sparse.SparseGlobalLayer(16, mode="topk", retention=0.25, kernel="tcgen05")
     a = layer(x.q, x.kp, x.vp, x.ks, x.vs).clone()

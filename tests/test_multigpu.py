@@ -19,6 +19,8 @@ def _free_port():
 
 def _worker(rank, world, port, result_q):
     import torch.distributed as dist
+    # one CTA per work item, so shard and full layer sum in the same order
+    os.environ["VGGT_ATTN_SPLIT"] = "1"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
