@@ -61,6 +61,32 @@ def allgather_frames(local, world, group=None):
     return buf.permute(1, 0, 2, 3).reshape(h, world * n, d)
 
 
+class PendingGather:
+    """An all-gather of frame shards in flight (``allgather_frames_async``).
+    ``result()`` makes the current stream wait for it and returns the
+    head-major [H, world * n_local, d] tensor."""
+
+    def __init__(self, buf, work):
+        self._buf, self._work = buf, work
+
+    def result(self):
+        self._work.wait()
+        w, h, n, d = self._buf.shape
+        return self._buf.permute(1, 0, 2, 3).reshape(h, w * n, d)
+
+
+def allgather_frames_async(local, world, group=None):
+    """``allgather_frames`` started asynchronously (NCCL runs it on its own
+    stream): work queued on the current stream before ``result()`` overlaps
+    the transfer."""
+    import torch.distributed as dist
+    h, n, d = local.shape
+    buf = torch.empty((world, h, n, d), device=local.device, dtype=local.dtype)
+    work = dist.all_gather_into_tensor(buf.view(-1), local.contiguous().view(-1), group=group,
+                                       async_op=True)
+    return PendingGather(buf, work)
+
+
 class QBlockShardedLayer:
     """The layer restricted to this rank's query blocks.
 

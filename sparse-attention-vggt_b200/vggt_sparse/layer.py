@@ -79,37 +79,52 @@ class SparseGlobalLayer:
             self._cache[key] = buf
         return buf
 
-    def __call__(self, q, kp, vp, ks, vs, out=None, events=None):
-        """Run the layer; ``events`` (3 CUDA events) are recorded before the
-        estimator, between estimator and attention, and after attention."""
+    def estimate(self, q, kp, n_special):
+        """The block-mask estimator alone (masks kept for ``attend``); needs
+        only q and the patch keys, so a caller can run it while V (or the
+        specials) are still arriving."""
         h, n, d = q.shape
         if h != self.heads:
             raise ValueError("layer built for %d heads, got %d" % (self.heads, h))
-        buf = self._buffers(q.device, n, kp.shape[1], ks.shape[1])
-        if out is None:
-            out = torch.empty_like(q)
-        if events is not None:
-            events[0].record()
+        buf = self._buffers(q.device, n, kp.shape[1], n_special)
         if self.sparse_heads:
             block_mask_estimate(q, kp, head_ids=buf["sparse_ids"], query_block=self.block,
                                 key_block=self.block, mode=self.mode, topk=buf["topk"],
                                 tau=self.tau, workspace=self.workspace,
                                 out=(buf["indices"], buf["counts"]))
+        self.last_masks = (buf["indices"], buf["counts"])
+        return buf
+
+    def attend(self, q, kp, vp, ks, vs, out=None):
+        """Block-sparse attention with the masks of the last ``estimate``."""
+        h, n, d = q.shape
+        buf = self._buffers(q.device, n, kp.shape[1], ks.shape[1])
+        if out is None:
+            out = torch.empty_like(q)
         evidence = None
         if self.evidence and self.sparse_heads:
             evidence = buf["evidence"]
             evidence.fill_(-math.inf)
-        if events is not None:
-            events[1].record()
         ops.launch_block_attention(q, kp, vp, ks, vs, buf["indices"], buf["counts"],
                                    buf["slot_ids"], head_dense=buf["dense_flags"],
                                    query_block=self.block, key_block=self.block, out=out,
                                    evidence=evidence, kernel=self.kernel,
                                    pair_qblocks=self.pair_qblocks, workspace=buf["attn_ws"])
-        if events is not None:
-            events[2].record()
         self.last_masks = (buf["indices"], buf["counts"])
         self.last_evidence = evidence
+        return out
+
+    def __call__(self, q, kp, vp, ks, vs, out=None, events=None):
+        """Run the layer; ``events`` (3 CUDA events) are recorded before the
+        estimator, between estimator and attention, and after attention."""
+        if events is not None:
+            events[0].record()
+        self.estimate(q, kp, ks.shape[1])
+        if events is not None:
+            events[1].record()
+        out = self.attend(q, kp, vp, ks, vs, out=out)
+        if events is not None:
+            events[2].record()
         return out
 
     def kept_flops(self, n_tokens, n_patch, n_special, dim):

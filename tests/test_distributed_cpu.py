@@ -58,43 +58,45 @@ def _worker(rank, world, port, result_q):
 
 
 def _work(rank, world, result_q):
-    if True:
-        import oracle
-        from vggt_sparse.synthetic import clustered_layer
-        x = clustered_layer(4, centres=16, heads=2, dim=32, patch_h=6, patch_w=6, seed=3,
-                            dtype=torch.float32)
-        per_frame_patch = 36
-        # frame-sharded K/V -> all-gather -> the full patch keys in frame-major order
-        f0, f1 = vd.frame_range(4, world, rank)
-        kp_local = x.kp[:, f0 * per_frame_patch:f1 * per_frame_patch]
-        kp_full = vd.allgather_frames(kp_local, world)
-        gather_ok = torch.equal(kp_full, x.kp)
-        # query-block shard of the oracle layer
-        n = x.shape.n_tokens
-        b0, b1 = vd.qblock_range(-(-n // 64), world, rank)
-        r0, r1 = b0 * 64, min(n, b1 * 64)
-        idx, cnt, _ = oracle.estimate_masks(x.q[:, r0:r1].numpy(), x.kp.numpy(), [0, 1], 64, 64,
-                                            "topk", 2, 32 ** -0.5)
-        out, _ = oracle.block_sparse_attention(x.q[:, r0:r1].numpy(), x.kp.numpy(),
-                                               x.vp.numpy(), x.ks.numpy(), x.vs.numpy(), idx, cnt,
+    import oracle
+    from vggt_sparse.synthetic import clustered_layer
+    x = clustered_layer(4, centres=16, heads=2, dim=32, patch_h=6, patch_w=6, seed=3,
+                        dtype=torch.float32)
+    per_frame_patch = 36
+    # frame-sharded K/V -> all-gather -> the full patch keys in frame-major order
+    f0, f1 = vd.frame_range(4, world, rank)
+    kp_local = x.kp[:, f0 * per_frame_patch:f1 * per_frame_patch]
+    kp_full = vd.allgather_frames(kp_local, world)
+    # the asynchronous form (the transfer overlaps work queued before result())
+    pending = vd.allgather_frames_async(x.vp[:, f0 * per_frame_patch:f1 * per_frame_patch], world)
+    vp_full = pending.result()
+    gather_ok = torch.equal(kp_full, x.kp) and torch.equal(vp_full, x.vp)
+    # query-block shard of the oracle layer
+    n = x.shape.n_tokens
+    b0, b1 = vd.qblock_range(-(-n // 64), world, rank)
+    r0, r1 = b0 * 64, min(n, b1 * 64)
+    idx, cnt, _ = oracle.estimate_masks(x.q[:, r0:r1].numpy(), x.kp.numpy(), [0, 1], 64, 64,
+                                        "topk", 2, 32 ** -0.5)
+    out, _ = oracle.block_sparse_attention(x.q[:, r0:r1].numpy(), x.kp.numpy(),
+                                           x.vp.numpy(), x.ks.numpy(), x.vs.numpy(), idx, cnt,
+                                           [0, 1])
+    rows = torch.tensor(out)
+    sizes = [torch.zeros(1, dtype=torch.long) for _ in range(world)]
+    dist.all_gather(sizes, torch.tensor([rows.shape[1]]))
+    padded = torch.zeros(2, max(int(s) for s in sizes), 32)
+    padded[:, :rows.shape[1]] = rows
+    parts = [torch.zeros_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded)
+    if rank == 0:
+        full = torch.cat([p[:, :int(s)] for p, s in zip(parts, sizes)], 1)
+        ref_idx, ref_cnt, _ = oracle.estimate_masks(x.q.numpy(), x.kp.numpy(), [0, 1], 64, 64,
+                                                    "topk", 2, 32 ** -0.5)
+        ref, _ = oracle.block_sparse_attention(x.q.numpy(), x.kp.numpy(), x.vp.numpy(),
+                                               x.ks.numpy(), x.vs.numpy(), ref_idx, ref_cnt,
                                                [0, 1])
-        rows = torch.tensor(out)
-        sizes = [torch.zeros(1, dtype=torch.long) for _ in range(world)]
-        dist.all_gather(sizes, torch.tensor([rows.shape[1]]))
-        padded = torch.zeros(2, max(int(s) for s in sizes), 32)
-        padded[:, :rows.shape[1]] = rows
-        parts = [torch.zeros_like(padded) for _ in range(world)]
-        dist.all_gather(parts, padded)
-        if rank == 0:
-            full = torch.cat([p[:, :int(s)] for p, s in zip(parts, sizes)], 1)
-            ref_idx, ref_cnt, _ = oracle.estimate_masks(x.q.numpy(), x.kp.numpy(), [0, 1], 64, 64,
-                                                        "topk", 2, 32 ** -0.5)
-            ref, _ = oracle.block_sparse_attention(x.q.numpy(), x.kp.numpy(), x.vp.numpy(),
-                                                   x.ks.numpy(), x.vs.numpy(), ref_idx, ref_cnt,
-                                                   [0, 1])
-            result_q.put((gather_ok, float(np.abs(full.numpy() - ref).max())))
-        else:
-            result_q.put((gather_ok, None))
+        result_q.put((gather_ok, float(np.abs(full.numpy() - ref).max())))
+    else:
+        result_q.put((gather_ok, None))
 
 
 def test_two_rank_gloo_sharding_reassembles_the_layer():
