@@ -97,7 +97,7 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
  * memory), it first pairs the query blocks of every indexed slot so that the
  * two selections of a tile differ least (three small kernels on `stream`),
  * which removes most of the masked tile work; the output is bit-identical
- * to the unpaired run.  When the grid is small (fewer than ~2,400 128-row
+ * to the unpaired run.  When the grid is small (fewer than 1,184 128-row
  * work items, e.g. one rank's query-block shard), the workspace also holds
  * partial results: each work item's key tiles are split over 2-4 CTAs and a
  * second launch merges them (output within rounding of the unsplit run; the

@@ -884,10 +884,11 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
 }
 
 int64_t attn_tc05_split(int64_t items) {
-  // enough CTAs for about 8 waves of 2 CTAs on 148 SMs, at most 4 splits
-  constexpr int64_t kTargetCtas = 8 * 2 * 148;
-  if (items <= 0 || items >= kTargetCtas) return 1;
-  const int64_t s = (kTargetCtas + items - 1) / items;
+  // grids of fewer than 4 waves (2 CTAs on each of 148 SMs) are split toward
+  // 8 waves, at most 4 ways; longer grids keep one CTA per item
+  constexpr int64_t kWave = 2 * 148;
+  if (items <= 0 || items >= 4 * kWave) return 1;
+  const int64_t s = (8 * kWave + items - 1) / items;
   return s > 4 ? 4 : s;
 }
 
