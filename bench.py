@@ -47,11 +47,14 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
-    p.add_argument("--component", choices=("layer", "assembly", "triton-ref"), default="layer",
+    p.add_argument("--component", choices=("layer", "assembly", "triton-ref", "token-ref"),
+                   default="layer",
                    help="layer: estimator + attention (the headline); assembly: mask "
                         "assembly with history and value order + the history update; "
                         "triton-ref: the reference's own Triton block_attention (installed "
-                        "in baseline/_ref) against this drop-in on the same inputs and masks")
+                        "in baseline/_ref) against this drop-in on the same inputs and masks; "
+                        "token-ref: per-token sparse attention, this library and (when "
+                        "installed) the reference's Triton kernels")
     return p.parse_args()
 
 
@@ -448,6 +451,68 @@ def run_triton_reference_comparison(args):
             "steps": args.steps, "warmup": args.warmup}), flush=True)
 
 
+def run_token_attention_bench(args):
+    """Per-token sparse attention on a dino_topk-like head: the 43,808 image
+    tokens of a 32-frame layer, each attending to 64 random keys of every
+    frame (top-k 2048, the reference's first kernel) or 128 (4096, its
+    online-softmax kernel).  Reports ms and the gathered K/V bytes per second;
+    the reference's Triton kernels run beside it when baseline/_ref has them."""
+    import vggt_sparse
+    ref = None
+    try:
+        sys.path.insert(0, os.path.join(REPO, "baseline", "_ref"))
+        from saf3r.triton import sparse_topk_attention as ref
+    except Exception:
+        ref = None
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    frames, per, d = 32, 1369, 64
+    n = frames * per
+    q = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
+
+    def timeit(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+    for per_frame in (64, 128):
+        topk = frames * per_frame
+        base = torch.arange(frames, device=dev, dtype=torch.int32) * per
+        idx = (torch.randint(0, per, (n, frames, per_frame), device=dev, generator=g,
+                             dtype=torch.int32) + base[None, :, None]).reshape(n, topk)
+        t_us = timeit(lambda: vggt_sparse.token_sparse_attention(q, k, v, idx))
+        line = {"component": "token-ref", "unit": "ms",
+                "workload": "%d queries x top-k %d (%d per frame x %d frames), dim %d, bf16"
+                            % (n, topk, per_frame, frames, d),
+                "ours_ms": t_us,
+                "gather_gbs": n * topk * 2 * d * 2 / (t_us * 1e-3) / 1e9,
+                "steps": args.steps, "warmup": args.warmup}
+        if ref is not None:
+            fn = (ref.fused_sparse_topk_attention if topk <= 2048
+                  else ref.fused_sparse_topk_attention_2)
+            o_ref = fn(q, k, v, idx)
+            o_us = vggt_sparse.token_sparse_attention(q, k, v, idx)
+            line["reference_kernel"] = fn.__name__
+            line["reference_triton_ms"] = timeit(lambda: fn(q, k, v, idx))
+            line["speedup"] = line["reference_triton_ms"] / t_us
+            line["max_abs_out_diff"] = (o_ref.float() - o_us.float()).abs().max().item()
+        else:
+            line["reference_triton_ms"] = None
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
@@ -461,6 +526,10 @@ def main():
     if args.component == "triton-ref":
         if rank == 0:
             run_triton_reference_comparison(args)
+        return
+    if args.component == "token-ref":
+        if rank == 0:
+            run_token_attention_bench(args)
         return
     import vggt_sparse
     from vggt_sparse import ops

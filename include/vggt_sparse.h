@@ -123,6 +123,27 @@ size_t vggt_block_attention_workspace_size(int64_t n_tokens, int64_t n_patch, in
                                            int block_q, int block_k);
 
 /*
+ * Per-token sparse attention.  Replaces saf3r/triton/sparse_topk_attention.py:115-166
+ * (fused_sparse_topk_attention) and :261-286 (fused_sparse_topk_attention_2,
+ * its online-softmax form for top-k above 2048): each query attends to its
+ * own key list, out[n] = softmax_j(q_n . k[idx[n, j]] * scale) . v[idx[n, j]],
+ * fp32 softmax and accumulation, any topk.
+ *
+ * q            [n_queries, dim], k and v [n_keys, dim], out [n_queries, dim]:
+ *              bf16 or fp16, contiguous, 16-byte aligned; dim 32, 64 or 128
+ * indices      int32; query r's list starts at indices + r * index_stride
+ *              (index_stride 0 = one list shared by every query, as the
+ *              reference's stride-zero expanded view); duplicates count twice
+ * Entries outside [0, n_keys) are skipped and set VGGT_STATUS_BAD_INDEX in
+ * *status (the reference reads them unchecked); a query with no valid entry
+ * gets zeros.
+ */
+int vggt_token_sparse_attention(const void* q, const void* k, const void* v,
+                                const int32_t* indices, int64_t index_stride, int64_t n_queries,
+                                int64_t n_keys, int64_t topk, int dim, int dtype, float scale,
+                                void* out, int32_t* status, void* stream);
+
+/*
  * Mask assembly with history and value order.  Replaces
  * saf3r/patch/adaptive_block_value.py:42-91 (select_block_mask), run there per
  * head in Python, for every (slot, query block) row in one launch.

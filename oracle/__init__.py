@@ -11,6 +11,10 @@ global-attention path of Liangyu-Xiang/Sparse-Attention-VGGT (SAF3R):
   saf3r/triton/adaptive_block_attention.py:7-60; tests/test_adaptive_block_value.py:172-184)
 * ``layout``     frame-major patch/special split
   (saf3r/patch/value_evolving_attention.py:17-20)
+* ``assembly``   select_block_mask with history and value order, and the
+  same-pass history update (saf3r/patch/adaptive_block_value.py:42-91, :389-396)
+* ``token_attention``  per-token sparse attention
+  (saf3r/triton/sparse_topk_attention.py:115-166, :261-286)
 
 It is the CHECKER: only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it.
@@ -23,3 +27,4 @@ from .attention import block_sparse_attention, dense_attention  # noqa: F401
 from .estimator import (block_mean, pooled_scores, select_mass, select_topk,  # noqa: F401
                         estimate_masks, mass_weights, topk_budget, score_keys)
 from .layout import token_layout  # noqa: F401
+from .token_attention import token_sparse_attention  # noqa: F401

@@ -188,6 +188,40 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
                                  nullptr, 0);
 }
 
+int vggt_token_sparse_attention(const void* q, const void* k, const void* v,
+                                const int32_t* indices, int64_t index_stride, int64_t n_queries,
+                                int64_t n_keys, int64_t topk, int dim, int dtype, float scale,
+                                void* out, int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (dtype != VGGT_DTYPE_BF16 && dtype != VGGT_DTYPE_FP16)
+    return fail("per-token sparse attention takes BF16 or FP16 (dtype code %d)", dtype);
+  if (dim != 32 && dim != 64 && dim != 128) return fail("head dim %d unsupported (32, 64, 128)", dim);
+  if (n_queries < 0 || n_keys < 0 || topk < 0 || index_stride < 0)
+    return fail("negative size argument");
+  if (!std::isfinite(scale)) return fail("scale must be finite");
+  if (n_queries == 0) return 0;
+  if (n_queries > (int64_t)0x7fffffff * 8) return fail("too many queries");
+  if (!q || !k || !v || !out || (topk > 0 && !indices))
+    return fail("q, k, v, out and indices must be non-NULL");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail("q/k/v/out must be 16-byte aligned");
+  vggt::TokenAttnArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.indices = indices;
+  a.index_stride = index_stride;
+  a.n_queries = n_queries;
+  a.n_keys = n_keys;
+  a.topk = topk;
+  a.dim = dim;
+  a.dtype = dtype;
+  a.scale = scale;
+  a.out = out;
+  a.status = status;
+  return cuda_rc(vggt::launch_token_attention(a, static_cast<cudaStream_t>(stream)));
+}
+
 int vggt_block_mask_assemble(const float* scores, int64_t n_slots, int64_t n_qblocks,
                              int64_t n_blocks, const int32_t* value_order, const int32_t* counts,
                              const int32_t* attention_counts, const int32_t* history,

@@ -76,6 +76,20 @@ cudaError_t launch_history_update(const float* evidence, const int32_t* ids, int
                                   const int32_t* keeps, int32_t* out, int64_t out_len,
                                   cudaStream_t stream);
 
+// token_attention.cu: per-token sparse attention
+struct TokenAttnArgs {
+  const void* q;        // [n_queries, dim]
+  const void* k;        // [n_keys, dim]
+  const void* v;        // [n_keys, dim]
+  const int32_t* indices;  // row r at indices + r * index_stride, topk entries
+  int64_t index_stride, n_queries, n_keys, topk;
+  int dim, dtype;
+  float scale;
+  void* out;            // [n_queries, dim]
+  int32_t* status;
+};
+cudaError_t launch_token_attention(const TokenAttnArgs& a, cudaStream_t stream);
+
 // attn_mma.cu
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu

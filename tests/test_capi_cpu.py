@@ -30,7 +30,7 @@ def test_header_declares_the_documented_entry_points():
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
         "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
         "vggt_block_select", "vggt_history_update", "vggt_sparse_last_error",
-        "vggt_sparse_version"])
+        "vggt_sparse_version", "vggt_token_sparse_attention"])
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -135,6 +135,18 @@ def test_assemble_and_history_argument_errors(lib):
         **kw).values())
     assert hist(ev=None) < 0
     assert hist(hlen=0) == 0
+
+
+def test_token_attention_argument_errors(lib):
+    call = lambda **kw: lib.vggt_token_sparse_attention(*dict(dict(
+        q=16, k=16, v=16, idx=16, stride=4, n=8, nk=100, topk=4, dim=64, dtype=0,
+        scale=0.125, out=16, status=None, stream=None), **kw).values())
+    for bad, msg in ((dict(dtype=3), "BF16 or FP16"), (dict(dim=48), "head dim"),
+                     (dict(topk=-1), "negative"), (dict(scale=float("nan")), "finite"),
+                     (dict(q=None), "non-NULL"), (dict(v=8), "aligned")):
+        assert call(**bad) < 0
+        assert msg in lib.vggt_sparse_last_error().decode()
+    assert call(n=0) == 0
 
 
 def test_select_argument_errors(lib):
