@@ -550,13 +550,20 @@ def main():
                                              x.shape.n_blocks, cfg.block)
     out = torch.empty_like(q)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
-    # estimator (pool Q, pool K, score + select), query-block pairing (bitmaps,
-    # window costs, greedy) when the tcgen05 kernel runs paired, attention
+    # estimator (pool Q, pool K, score + select), then, when the tcgen05 kernel
+    # runs with its workspace, query-block pairing (bitmaps, window costs,
+    # greedy, schedule), attention, and the merge launch of a key-range split
+    # (grids under 4 waves of 296 CTAs, or VGGT_ATTN_SPLIT > 1)
     launches_per_step = (3 if layer.sparse_heads else 0) + 1
+    n_slots = len(layer.sparse_heads) + len(layer.dense_heads)
     if layer.sparse_heads and layer.pair_qblocks and args.kernel != "mma_sync" and \
-            ops.attention_workspace_size(q.shape[1], kp.shape[1], len(layer.sparse_heads) +
-                                         len(layer.dense_heads)) > 0:
-        launches_per_step += 3
+            ops.attention_workspace_size(q.shape[1], kp.shape[1], n_slots) > 0:
+        launches_per_step += 4
+        items = n_slots * ((-(-q.shape[1] // cfg.block) + 1) // 2)
+        forced = os.environ.get("VGGT_ATTN_SPLIT", "")
+        split = int(forced) if forced in ("1", "2", "3", "4") else (2 if items < 4 * 296 else 1)
+        if split > 1:
+            launches_per_step += 1
 
     gather = None
     if args.shard == "kv-allgather" and world > 1:
