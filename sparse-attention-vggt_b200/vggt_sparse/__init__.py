@@ -14,6 +14,7 @@ from .configs import CONFIGS, LayerConfig  # noqa: F401
 from .estimator import BlockMasks, block_mask_estimate, block_select  # noqa: F401
 from .layer import SparseGlobalLayer, topk_budget  # noqa: F401
 from .layout import LayerShape, split_keys, token_layout  # noqa: F401
+from .pipeline import HostPipeline  # noqa: F401
 from .token_attention import token_sparse_attention  # noqa: F401
 from .profile import dense_heads_from_decisions, dense_heads_from_profile, split_heads  # noqa: F401
 
