@@ -47,14 +47,16 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
-    p.add_argument("--component", choices=("layer", "assembly", "triton-ref", "token-ref"),
+    p.add_argument("--component",
+                   choices=("layer", "assembly", "triton-ref", "token-ref", "qk-topk"),
                    default="layer",
                    help="layer: estimator + attention (the headline); assembly: mask "
                         "assembly with history and value order + the history update; "
                         "triton-ref: the reference's own Triton block_attention (installed "
                         "in baseline/_ref) against this drop-in on the same inputs and masks; "
                         "token-ref: per-token sparse attention, this library and (when "
-                        "installed) the reference's Triton kernels")
+                        "installed) the reference's Triton kernels; qk-topk: per-frame QK "
+                        "top-k, this library and the reference's Triton kernel")
     return p.parse_args()
 
 
@@ -513,6 +515,97 @@ def run_token_attention_bench(args):
         print(json.dumps(line), flush=True)
 
 
+def run_qk_topk_bench(args):
+    """Per-frame QK top-k of the lazy correspondence head: the 43,808 image
+    tokens of a 32-frame layer (37 x 37 patches per frame), head dim 64,
+    top-4 per frame (the reference's lazy_dino_topk setting), plus top-16 and
+    top-64.  Reports ms, the scores per second and the tensor roofline of the
+    QK^T FLOPs; the reference's Triton kernel (baseline/_ref) runs beside it
+    on the same inputs, once through its public function and once as the bare
+    kernel launch that function makes."""
+    import contextlib
+    import io
+    import vggt_sparse
+    ref = None
+    try:
+        sys.path.insert(0, os.path.join(REPO, "baseline", "_ref"))
+        from saf3r.triton import fused_qk_topk as ref
+        import triton
+    except Exception:
+        ref = None
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    frames, per, d = 32, 1369, 64
+    n = frames * per
+    q = torch.randn(1, n, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, n, d, device=dev, generator=g).to(torch.bfloat16)
+    peaks = load_peaks()
+    peak = peaks.get("bf16_tflops") if peaks else None
+
+    def timeit(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    flops = 2.0 * n * n * d
+    for topk in (4, 16, 64):
+        ours = lambda: vggt_sparse.compute_qk_topk_indices_fused(q, k, topk, num_toks_per_img=per)
+        t_ms = timeit(ours)
+        tf = flops / (t_ms * 1e-3) / 1e12
+        line = {"component": "qk-topk", "unit": "ms",
+                "workload": "%d queries x %d keys (%d frames of %d), dim %d, top-%d per frame, bf16"
+                            % (n, n, frames, per, d, topk),
+                "ours_ms": t_ms, "scores_per_s": n * n / (t_ms * 1e-3),
+                "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                             "frac": tf / peak if peak else None,
+                             "note": "QK^T FLOPs 2*Nq*Nk*D over the call; of measured bf16 burst"},
+                "steps": args.steps, "warmup": args.warmup}
+        if ref is not None:
+            quiet = contextlib.redirect_stdout(io.StringIO())
+            with quiet:
+                want = ref.compute_qk_topk_indices_fused(q, k, topk, num_toks_per_img=per)
+            got = ours()
+            line["equal_fraction_vs_reference"] = (got == want).float().mean().item()
+
+            def public():
+                with contextlib.redirect_stdout(io.StringIO()):
+                    ref.compute_qk_topk_indices_fused(q, k, topk, num_toks_per_img=per)
+            line["reference_public_ms"] = timeit(public)
+            # the bare kernel launch of that function (its padding and
+            # launch parameters, fused_qk_topk.py:166-199)
+            te = min(topk, per)
+            kv = triton.next_power_of_2(te)
+            bn = max(64, kv)
+            pad = (bn - per % bn) % bn
+            kp = torch.nn.functional.pad(k.view(1, frames, per, d), (0, 0, 0, pad)).reshape(
+                1, frames * (per + pad), d)
+            out = torch.full((1, n, frames * kv), -1, device=dev, dtype=torch.int32)
+            grid = (triton.cdiv(n, 64), 1)
+
+            def bare():
+                ref._fused_perframe_qk_topk_kernel[grid](
+                    q, kp, out, q.stride(0), q.stride(1), q.stride(2), kp.stride(0),
+                    kp.stride(1), kp.stride(2), out.stride(0), out.stride(1), out.stride(2),
+                    n, frames * (per + pad), d, per, segment_len=per + pad, BLOCK_M=64,
+                    BLOCK_N=bn, BLOCK_DMODEL=triton.next_power_of_2(d), K_VAL=kv, num_warps=8,
+                    num_stages=2)
+            line["reference_kernel_ms"] = timeit(bare)
+            line["speedup_vs_reference_kernel"] = line["reference_kernel_ms"] / t_ms
+            line["speedup_vs_reference_public"] = line["reference_public_ms"] / t_ms
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
@@ -530,6 +623,10 @@ def main():
     if args.component == "token-ref":
         if rank == 0:
             run_token_attention_bench(args)
+        return
+    if args.component == "qk-topk":
+        if rank == 0:
+            run_qk_topk_bench(args)
         return
     import vggt_sparse
     from vggt_sparse import ops

@@ -144,6 +144,27 @@ int vggt_token_sparse_attention(const void* q, const void* k, const void* v,
                                 void* out, int32_t* status, void* stream);
 
 /*
+ * Per-frame QK top-k.  Replaces saf3r/triton/fused_qk_topk.py:128-217
+ * (compute_qk_topk_indices_fused) and its kernel _fused_perframe_qk_topk_kernel
+ * (:24-108): for every query row and every frame of `tokens` consecutive keys,
+ * the global indices of the frame's min(topk, tokens) largest scores q . k
+ * (fp32 accumulation of the bf16 inputs, no scaling), in descending order,
+ * ties to the lower key index; scores order as their sortable 32-bit keys
+ * (the float order with +0 above -0).
+ *
+ * q      [batch, n_queries, dim] bf16, contiguous, 16-byte aligned
+ * k      [batch, frames * tokens, dim] bf16, contiguous, 16-byte aligned
+ * out    [batch, n_queries, frames * min(topk, tokens)] int32, 16-byte aligned;
+ *        frame f's entries are keys f * tokens .. (f + 1) * tokens - 1
+ * dim    64 or 128 (callers zero-pad other head dims: the scores are unchanged)
+ * topk   1..128 after clamping to tokens
+ * groups frame groups per 128-row query tile (0 = automatic)
+ */
+int vggt_frame_qk_topk(const void* q, const void* k, int32_t* out, int64_t batch,
+                       int64_t n_queries, int64_t frames, int64_t tokens, int dim, int64_t topk,
+                       int64_t groups, int32_t* status, void* stream);
+
+/*
  * Mask assembly with history and value order.  Replaces
  * saf3r/patch/adaptive_block_value.py:42-91 (select_block_mask), run there per
  * head in Python, for every (slot, query block) row in one launch.

@@ -15,6 +15,8 @@ global-attention path of Liangyu-Xiang/Sparse-Attention-VGGT (SAF3R):
   same-pass history update (saf3r/patch/adaptive_block_value.py:42-91, :389-396)
 * ``token_attention``  per-token sparse attention
   (saf3r/triton/sparse_topk_attention.py:115-166, :261-286)
+* ``frame_topk``  per-frame QK top-k (saf3r/triton/fused_qk_topk.py:24-217,
+  saf3r/triton/topk_utils.py:24-28)
 
 It is the CHECKER: only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it.
@@ -28,3 +30,4 @@ from .estimator import (block_mean, pooled_scores, select_mass, select_topk,  # 
                         estimate_masks, mass_weights, topk_budget, score_keys)
 from .layout import token_layout  # noqa: F401
 from .token_attention import token_sparse_attention  # noqa: F401
+from .frame_topk import qk_topk_per_frame, score_keys32  # noqa: F401

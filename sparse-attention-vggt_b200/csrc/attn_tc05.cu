@@ -802,6 +802,21 @@ static bool make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads
 
 }  // namespace tcattn
 
+bool encode_tmap_3d_sw128(CUtensorMap* map, const void* ptr, int dtype, int64_t d0, int64_t d1,
+                          int64_t d2, uint32_t box0, uint32_t box1) {
+  tcattn::EncodeTiledFn fn = tcattn::encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  const cuuint64_t strides[2] = {(cuuint64_t)d0 * 2, (cuuint64_t)(d0 * d1) * 2};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == VGGT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool attn_tc05_supported(const AttnArgs& a) {
   return a.dim == 64 && a.block_q == 64 && a.block_k == 64 && a.n_patch >= 1 &&
          a.scale > 0.f && a.nb <= 65536 && a.max_blocks <= 65536 && a.n_tokens <= 0x7fffffffLL &&

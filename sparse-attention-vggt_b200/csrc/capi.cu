@@ -222,6 +222,37 @@ int vggt_token_sparse_attention(const void* q, const void* k, const void* v,
   return cuda_rc(vggt::launch_token_attention(a, static_cast<cudaStream_t>(stream)));
 }
 
+int vggt_frame_qk_topk(const void* q, const void* k, int32_t* out, int64_t batch,
+                       int64_t n_queries, int64_t frames, int64_t tokens, int dim, int64_t topk,
+                       int64_t groups, int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (batch < 0 || n_queries < 0 || frames < 0 || tokens < 1 || topk < 1 || groups < 0)
+    return fail("batch, n_queries, frames, groups must be >= 0 and tokens, topk >= 1");
+  if (topk > tokens) topk = tokens;
+  if (!vggt::frame_topk_supported(dim, topk))
+    return fail("dim %d / topk %lld unsupported (dim 64 or 128, topk <= 128)", dim,
+                (long long)topk);
+  if (batch == 0 || n_queries == 0 || frames == 0) return 0;
+  if (n_queries > 0x7fffffffLL || frames * tokens > 0x7fffffffLL || batch > 0x7fffffffLL)
+    return fail("sizes above 2^31 rows are not supported");
+  if (!q || !k || !out) return fail("q, k and out must be non-NULL");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(out))
+    return fail("q/k/out must be 16-byte aligned");
+  vggt::FrameTopkArgs a;
+  a.q = q;
+  a.k = k;
+  a.out = out;
+  a.status = status;
+  a.batch = batch;
+  a.n_queries = n_queries;
+  a.frames = frames;
+  a.tokens = tokens;
+  a.topk = topk;
+  a.dim = dim;
+  a.groups = groups;
+  return cuda_rc(vggt::launch_frame_topk(a, static_cast<cudaStream_t>(stream)));
+}
+
 int vggt_block_mask_assemble(const float* scores, int64_t n_slots, int64_t n_qblocks,
                              int64_t n_blocks, const int32_t* value_order, const int32_t* counts,
                              const int32_t* attention_counts, const int32_t* history,

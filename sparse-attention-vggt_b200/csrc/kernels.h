@@ -90,6 +90,19 @@ struct TokenAttnArgs {
 };
 cudaError_t launch_token_attention(const TokenAttnArgs& a, cudaStream_t stream);
 
+// frame_topk.cu: per-frame QK top-k
+struct FrameTopkArgs {
+  const void* q;       // [batch, n_queries, dim] bf16
+  const void* k;       // [batch, frames * tokens, dim] bf16
+  int32_t* out;        // [batch, n_queries, frames * topk]
+  int32_t* status;
+  int64_t batch, n_queries, frames, tokens, topk;
+  int dim;
+  int64_t groups;      // frame groups per query tile (0 = automatic)
+};
+bool frame_topk_supported(int dim, int64_t topk);
+int64_t frame_topk_groups(int64_t frames, int64_t work_rows);
+cudaError_t launch_frame_topk(const FrameTopkArgs& a, cudaStream_t stream);
 // attn_mma.cu
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu

@@ -232,4 +232,11 @@ __device__ __forceinline__ void tmem_wait_st() {
 #undef VGGT_W8
 
 }  // namespace tc
+
+// Host: 3-D tensor map [d2][d1][d0] of 2-byte elements (VGGT_DTYPE_*), box
+// (box0, box1, 1), 128-byte swizzle, zero fill out of bounds.  False when the
+// driver entry point is unavailable or the driver rejects the arguments.
+bool encode_tmap_3d_sw128(CUtensorMap* map, const void* ptr, int dtype, int64_t d0, int64_t d1,
+                          int64_t d2, uint32_t box0, uint32_t box1);
+
 }  // namespace vggt

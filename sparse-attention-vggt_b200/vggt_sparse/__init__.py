@@ -12,6 +12,7 @@ from .assembly import assemble_masks, history_update, select_block_mask  # noqa:
 from .block_attention import block_attention  # noqa: F401
 from .configs import CONFIGS, LayerConfig  # noqa: F401
 from .estimator import BlockMasks, block_mask_estimate, block_select  # noqa: F401
+from .frame_topk import compute_qk_topk_indices_fused  # noqa: F401
 from .layer import SparseGlobalLayer, topk_budget  # noqa: F401
 from .layout import LayerShape, split_keys, token_layout  # noqa: F401
 from .pipeline import HostPipeline  # noqa: F401

@@ -29,6 +29,7 @@ SIGNATURES = {
     "vggt_block_attention_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I, _I]),
     "vggt_token_sparse_attention": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I,
                                          ctypes.c_float, _P, _P, _P]),
+    "vggt_frame_qk_topk": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _I64, _I64, _P, _P]),
     "vggt_block_mask_assemble": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64,
                                       _P, _P]),
     "vggt_history_update": (_I, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P]),

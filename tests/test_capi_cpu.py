@@ -29,7 +29,7 @@ def test_header_declares_the_documented_entry_points():
     assert declared_symbols() == sorted([
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
         "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
-        "vggt_block_select", "vggt_history_update", "vggt_sparse_last_error",
+        "vggt_block_select", "vggt_frame_qk_topk", "vggt_history_update", "vggt_sparse_last_error",
         "vggt_sparse_version", "vggt_token_sparse_attention"])
 
 
@@ -147,6 +147,32 @@ def test_token_attention_argument_errors(lib):
         assert call(**bad) < 0
         assert msg in lib.vggt_sparse_last_error().decode()
     assert call(n=0) == 0
+
+
+def test_frame_topk_argument_errors(lib):
+    call = lambda **kw: lib.vggt_frame_qk_topk(*dict(dict(
+        q=16, k=16, out=16, batch=1, nq=8, frames=2, tokens=100, dim=64, topk=4, groups=0,
+        status=None, stream=None), **kw).values())
+    for bad, msg in ((dict(dim=48), "unsupported"), (dict(topk=129, tokens=200), "unsupported"),
+                     (dict(tokens=0), "tokens"), (dict(groups=-1), ">= 0"),
+                     (dict(q=None), "non-NULL"), (dict(out=8), "aligned")):
+        assert call(**bad) < 0, bad
+        assert msg in lib.vggt_sparse_last_error().decode()
+    assert call(nq=0) == 0 and call(frames=0) == 0
+    assert call(topk=500, tokens=100, q=None) < 0  # clamped to 100, then the pointer check
+    assert "non-NULL" in lib.vggt_sparse_last_error().decode()
+
+
+def test_frame_topk_python_checks():
+    import torch
+    import vggt_sparse
+    q = torch.zeros(1, 4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        vggt_sparse.compute_qk_topk_indices_fused(q, q, 2, num_toks_per_img=2)
+    with pytest.raises(AssertionError):
+        vggt_sparse.compute_qk_topk_indices_fused(q, q, 2, num_toks_per_img=3)
+    with pytest.raises(AssertionError):
+        vggt_sparse.compute_qk_topk_indices_fused(q, q, 2)
 
 
 def test_select_argument_errors(lib):
