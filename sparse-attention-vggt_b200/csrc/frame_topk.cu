@@ -18,10 +18,10 @@
 //  * warps 2-5: selection, one query row per thread (TMEM lane = row).  A
 //    score passes if it is not below the row's current k-th best; passing
 //    scores are appended to a per-row candidate buffer with predicated
-//    shared-memory stores (no branch per score).  Every 16 columns the
-//    candidates are merged into the row's sorted list: registers for
-//    topk <= 8, shared memory above.  After a frame's last tile the list is
-//    written out and reset.
+//    shared-memory stores (no branch per score).  Every 32 columns the
+//    candidates are merged into the row's list: a sorted list in registers
+//    for topk <= 8, a min-heap in shared memory above.  After a frame's last
+//    tile the list is written out (in descending order) and reset.
 //
 // Every mbarrier wait is bounded (1 s); on expiry the CTA raises its abort
 // flag, records VGGT_STATUS_TIMEOUT, drains its in-flight copies, frees its
@@ -41,7 +41,7 @@ namespace qktopk {
 constexpr int BM = 128;                     // query rows per CTA
 constexpr int BN = 128;                     // keys per tile
 constexpr int THREADS = 192;
-constexpr int CHUNK = 16;                   // columns between merges
+constexpr int CHUNK = 32;                   // columns between merges
 constexpr int MAX_STAGES = 4;
 constexpr uint32_t SPAN_BYTES = 128 * 128;  // 128 rows x 64 bf16: one 128-B swizzle span wide
 constexpr uint32_t CAND_BYTES = CHUNK * BM * 8;
@@ -165,33 +165,55 @@ struct RegList {  // topk <= KR <= 8: registers
   }
 };
 
-struct SmemList {  // topk <= 128: shared memory, [slot][row] so a warp's rows are contiguous
-  uint32_t* key;
-  uint32_t* idx;
+// topk <= 128: a min-heap in shared memory ([slot][row], so a warp's rows are
+// contiguous) of 64-bit composites (key << 32 | ~index): the root is the
+// row's current k-th best.  An insert replaces the root and sifts it down;
+// the frame's list is heap-sorted into descending order when written out.
+// Slots start at composite 0, below every real entry.
+struct HeapList {
+  unsigned long long* h;
   int k, row;
-  uint32_t tail;
+  uint32_t root_key;
   __device__ __forceinline__ void reset() {
-    for (int i = 0; i < k; ++i) key[i * BM + row] = 0u;
-    tail = 0u;
+    for (int i = 0; i < k; ++i) h[i * BM + row] = 0ull;
+    root_key = 0u;
   }
-  __device__ __forceinline__ uint32_t last() const { return tail; }
-  __device__ __forceinline__ void insert(uint32_t kn, uint32_t ix) {
-    int i = k - 1;
-    while (i > 0) {
-      const uint32_t kp = key[(i - 1) * BM + row];
-      if (kp >= kn) break;
-      key[i * BM + row] = kp;
-      idx[i * BM + row] = idx[(i - 1) * BM + row];
-      --i;
+  __device__ __forceinline__ uint32_t last() const { return root_key; }
+  __device__ __forceinline__ void sift(unsigned long long c, int i, int n) {
+    while (true) {
+      const int l = 2 * i + 1;
+      if (l >= n) break;
+      unsigned long long cc = h[l * BM + row];
+      int child = l;
+      if (l + 1 < n) {
+        const unsigned long long cr = h[(l + 1) * BM + row];
+        if (cr < cc) {
+          cc = cr;
+          child = l + 1;
+        }
+      }
+      if (cc >= c) break;
+      h[i * BM + row] = cc;
+      i = child;
     }
-    key[i * BM + row] = kn;
-    idx[i * BM + row] = ix;
-    tail = key[(k - 1) * BM + row];
+    h[i * BM + row] = c;
   }
-  __device__ __forceinline__ void write(int32_t* dst, int topk, int32_t base) const {
+  // requires kn > last(): the new entry beats the root
+  __device__ __forceinline__ void insert(uint32_t kn, uint32_t ix) {
+    sift(((unsigned long long)kn << 32) | (unsigned long long)(0xffffffffu - ix), 0, k);
+    root_key = (uint32_t)(h[row] >> 32);
+  }
+  // heap-sorts in place (descending from slot 0) and writes the first topk
+  __device__ __forceinline__ void write(int32_t* dst, int topk, int32_t base) {
+    for (int n = k - 1; n > 0; --n) {
+      const unsigned long long top = h[row];
+      const unsigned long long tail = h[n * BM + row];
+      h[n * BM + row] = top;
+      sift(tail, 0, n);
+    }
     for (int i = 0; i < topk; ++i) {
-      const uint32_t kk = key[i * BM + row];
-      dst[i] = kk ? base + (int32_t)idx[i * BM + row] : -1;
+      const unsigned long long c = h[i * BM + row];
+      dst[i] = c ? base + (int32_t)(0xffffffffu - (uint32_t)c) : -1;
     }
   }
 };
@@ -318,10 +340,9 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int64_t qrow = qt * BM + row;
     const bool valid_row = qrow < p.n_queries;
     const uint32_t cand_row = base + p.off_cand + (uint32_t)row * 8u;
-    typename std::conditional<(KR > 0), RegList<(KR > 0 ? KR : 1)>, SmemList>::type list;
+    typename std::conditional<(KR > 0), RegList<(KR > 0 ? KR : 1)>, HeapList>::type list;
     if constexpr (KR == 0) {
-      list.key = reinterpret_cast<uint32_t*>(sbase + p.off_list);
-      list.idx = list.key + (size_t)p.topk * BM;
+      list.h = reinterpret_cast<unsigned long long*>(sbase + p.off_list);
       list.k = p.topk;
       list.row = row;
     }
