@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
     p.add_argument("--component",
-                   choices=("layer", "assembly", "triton-ref", "token-ref", "qk-topk"),
+                   choices=("layer", "assembly", "triton-ref", "token-ref", "qk-topk",
+                            "aggregator"),
                    default="layer",
                    help="layer: estimator + attention (the headline); assembly: mask "
                         "assembly with history and value order + the history update; "
@@ -56,7 +57,9 @@ def parse_args():
                         "in baseline/_ref) against this drop-in on the same inputs and masks; "
                         "token-ref: per-token sparse attention, this library and (when "
                         "installed) the reference's Triton kernels; qk-topk: per-frame QK "
-                        "top-k, this library and the reference's Triton kernel")
+                        "top-k, this library and the reference's Triton kernel; aggregator: "
+                        "config 3, the reference's VGGT aggregator end to end with its "
+                        "Triton operator and with this drop-in")
     return p.parse_args()
 
 
@@ -606,6 +609,176 @@ def run_qk_topk_bench(args):
         print(json.dumps(line), flush=True)
 
 
+def reference_stubs():
+    """Stand-ins for two packages the reference imports at module load
+    (addict in saf3r/patch, omegaconf in its DA3 model) that this image does
+    not have; the VGGT path run here uses neither beyond those imports."""
+    import types
+    try:
+        import addict  # noqa: F401
+    except ImportError:
+        m = types.ModuleType("addict")
+
+        class Dict(dict):
+            def __getattr__(self, key):
+                try:
+                    return self[key]
+                except KeyError as e:
+                    raise AttributeError(key) from e
+
+            def __setattr__(self, key, value):
+                self[key] = value
+        m.Dict = Dict
+        sys.modules["addict"] = m
+    try:
+        import omegaconf  # noqa: F401
+    except ImportError:
+        m = types.ModuleType("omegaconf")
+
+        class OmegaConf:
+            @staticmethod
+            def register_new_resolver(*a, **k):
+                return None
+
+            @staticmethod
+            def create(*a, **k):
+                raise NotImplementedError("omegaconf is not installed")
+            load = create
+        m.OmegaConf = OmegaConf
+        m.DictConfig = type("DictConfig", (dict,), {})
+        m.ListConfig = type("ListConfig", (list,), {})
+        sys.modules["omegaconf"] = m
+
+
+def build_reference_aggregator(device, seed=0, retention=0.25):
+    """The reference's VGGT Aggregator (saf3r/models/official_vggt/models/
+    aggregator.py: ViT-L/14 patch embed with 4 registers, 24 frame + 24
+    global blocks, dim 1024, 16 heads, RoPE-2D), random-init from `seed`, with
+    its global attention replaced by the reference's adaptive block attention
+    (saf3r/patch/adaptive_block_value.py:444-457) at a fixed top-k budget:
+    retention `retention`, no escalation (audit_guard off).  The attention
+    operator it calls is saf3r.triton.adaptive_block_attention.block_attention,
+    looked up at every call, so assigning that attribute swaps the backend."""
+    reference_stubs()
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    from saf3r.models.official_vggt.models.aggregator import Aggregator
+    from saf3r.patch.adaptive_block_value import install_adaptive_block_value
+    import saf3r.triton.adaptive_block_attention as ref_op
+    torch.manual_seed(seed)
+    model = torch.nn.Module()
+    with torch.device(device):  # initialise on the device (909M parameters)
+        model.aggregator = Aggregator()
+    model = model.to(device).eval()  # and the buffers made by legacy constructors
+    state = install_adaptive_block_value(model, retention=retention,
+                                         budget_candidates=(retention,), audit_guard=False,
+                                         profile_stages=True)
+    return model, state, ref_op
+
+
+def aggregator_forward(model, images):
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        out, _ = model.aggregator(images)
+    return out
+
+
+def run_aggregator_bench(args):
+    """Config 3: the reference's random-init VGGT aggregator end to end on 16
+    synthetic 518 x 518 views (a smooth random texture under random
+    homographies), global attention sparse at top-k 25 %, forward in bf16
+    autocast.  The same model and inputs run twice: with the reference's
+    Triton block_attention; with vggt_sparse.block_attention assigned in its
+    place; and with vggt_sparse.select_block_mask assigned as well.  The arms
+    alternate step by step.  Reports the forward time (dominated by the
+    reference module's host-side work, so noisy), the reference's own
+    per-stage times of its global-attention module summed over the 24 layers
+    (its profile_stages CUDA events), and how far the last block's output
+    moves."""
+    import vggt_sparse
+    from vggt_sparse.synthetic import homography_views
+    dev = torch.device("cuda", torch.cuda.current_device())
+    frames = 16
+    model, state, ref_op = build_reference_aggregator(dev)
+    images = homography_views(frames, 518, seed=3, device=dev)
+    triton_op = ref_op.block_attention
+    calls = {"n": 0}
+
+    def ours(*a, **k):
+        calls["n"] += 1
+        return vggt_sparse.block_attention(*a, **k)
+
+    import saf3r.patch.adaptive_block_value as abv
+    ref_select = abv.select_block_mask
+
+    def forward(arm):
+        _, op, select = arm
+        ref_op.block_attention = op
+        abv.select_block_mask = select
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        out = aggregator_forward(model, images)
+        e1.record()
+        torch.cuda.synchronize()
+        stages = {}
+        for r in state.records:
+            for k, v in r["stage_ms"].items():
+                stages[k] = stages.get(k, 0.0) + v
+        return e0.elapsed_time(e1), stages, out[-1].float()
+
+    # reference: its Triton operator and its PyTorch select_block_mask;
+    # ours: the drop-in operator; ours+assembly: also the device mask assembly
+    arms = (("reference", triton_op, ref_select), ("ours", ours, ref_select),
+            ("ours+assembly", ours, vggt_sparse.select_block_mask))
+    fwd = {a[0]: [] for a in arms}
+    stage = {a[0]: [] for a in arms}
+    last = {}
+    try:
+        for _ in range(args.warmup):
+            for arm in arms:
+                forward(arm)
+        calls["n"] = 0
+        for _ in range(args.steps):  # the arms alternate, step by step
+            for arm in arms:
+                t, st, last[arm[0]] = forward(arm)
+                fwd[arm[0]].append(t)
+                stage[arm[0]].append(st)
+    finally:
+        ref_op.block_attention = triton_op
+        abv.select_block_mask = ref_select
+
+    def med_stages(a):
+        return {k: statistics.median(st[k] for st in stage[a]) for k in stage[a][0]}
+    st_ref, st_us, st_as = med_stages("reference"), med_stages("ours"), med_stages("ours+assembly")
+    t_ref, t_us = statistics.median(fwd["reference"]), statistics.median(fwd["ours"])
+    s_ref, s_us = st_ref.get("sparse_attention", 0.0), st_us.get("sparse_attention", 0.0)
+    diff = (last["ours"] - last["reference"]).abs()
+    diff_as = (last["ours+assembly"] - last["reference"]).abs()
+    line = {"component": "aggregator", "unit": "ms",
+            "workload": "reference VGGT aggregator (random init, ViT-L/14 + 24 frame/24 global "
+                        "blocks), 16 views 518x518 (%d tokens), global attention top-k 25%%, "
+                        "bf16 autocast" % (frames * 1374),
+            "reference_forward_ms": t_ref, "ours_forward_ms": t_us,
+            "reference_sparse_attention_ms": s_ref, "ours_sparse_attention_ms": s_us,
+            "sparse_attention_speedup": s_ref / s_us if s_us else None,
+            "forward_speedup": t_ref / t_us,
+            "global_attention_stages_ms": {"reference": sum(st_ref.values()),
+                                           "ours": sum(st_us.values()),
+                                           "ours+assembly": sum(st_as.values())},
+            "mask_assembly_ms": {"reference": st_ref.get("mask_assembly"),
+                                 "ours+assembly": st_as.get("mask_assembly")},
+            "stage_ms_summed_over_global_layers": {"reference": st_ref, "ours": st_us,
+                                                   "ours+assembly": st_as},
+            "forward_ms_per_step": fwd,
+            "ours_calls_per_forward": calls["n"] / (2 * args.steps),
+            "ours+assembly_last_block_mean_rel_diff":
+                (diff_as.mean() / last["reference"].abs().mean()).item(),
+            "last_block_max_abs_diff": diff.max().item(),
+            "last_block_mean_rel_diff": (diff.mean() / last["reference"].abs().mean()).item(),
+            "steps": args.steps, "warmup": args.warmup}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
@@ -627,6 +800,10 @@ def main():
     if args.component == "qk-topk":
         if rank == 0:
             run_qk_topk_bench(args)
+        return
+    if args.component == "aggregator":
+        if rank == 0:
+            run_aggregator_bench(args)
         return
     import vggt_sparse
     from vggt_sparse import ops

@@ -2,7 +2,8 @@
 
 cfg1  4 frames, top-k 25% of key blocks, 64 centres (CPU-runnable case)
 cfg2  32 frames, softmax-mass 0.9, heads 0-3 dense, 128 centres (headline)
-cfg3  full 24+24-block aggregator at 16 frames, top-k 25% (aggregator.py)
+cfg3  16 frames, top-k 25% (one layer here; the full aggregator end to end is
+      bench.py --component aggregator, the reference's model with this drop-in)
 cfg4  100 frames, top-k 15%, 256 centres, head-sharded over 2/4/8 GPUs
 cfg5  256 frames, mass 0.85, heads 0-3 dense, 512 centres, query-block sharded
 """

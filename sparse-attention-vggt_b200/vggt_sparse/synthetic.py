@@ -66,3 +66,31 @@ def clustered_layer(frames, *, centres=64, heads=16, dim=64, patch_h=37, patch_w
     if not keep_full:
         k = v = None
     return LayerInputs(shape, q.contiguous(), k, v, kp, vp, ks, vs)
+
+
+def homography_views(frames, size=518, *, seed=0, device="cpu", texture=48, max_shift=0.08,
+                     max_persp=0.15):
+    """`frames` RGB views [1, S, 3, size, size] in [0, 1] of one smooth random
+    texture (low-pass noise: a `texture`^2 random grid upsampled bicubically),
+    each warped by its own random homography near the identity (translation
+    up to `max_shift` of the image, perspective terms up to `max_persp`), so
+    neighbouring views overlap the way a camera sweep's do."""
+    import torch.nn.functional as F
+    g = torch.Generator(device="cpu").manual_seed(int(seed))
+    base = torch.rand(1, 3, texture, texture, generator=g)
+    base = F.interpolate(base, size=(2 * size, 2 * size), mode="bicubic", align_corners=False)
+    base = base.clamp(0, 1).to(device)
+    ys, xs = torch.meshgrid(torch.linspace(-0.5, 0.5, size), torch.linspace(-0.5, 0.5, size),
+                            indexing="ij")
+    pts = torch.stack((xs, ys, torch.ones_like(xs)), -1).reshape(-1, 3)
+    views = []
+    for _ in range(frames):
+        hmat = torch.eye(3)
+        hmat[:2, :2] += (torch.rand(2, 2, generator=g) - 0.5) * 2 * max_persp
+        hmat[:2, 2] = (torch.rand(2, generator=g) - 0.5) * 2 * max_shift
+        hmat[2, :2] = (torch.rand(2, generator=g) - 0.5) * 2 * max_persp
+        w = pts @ hmat.T
+        grid = (w[:, :2] / w[:, 2:3]).reshape(1, size, size, 2).to(device)
+        views.append(F.grid_sample(base, grid, mode="bilinear", padding_mode="reflection",
+                                   align_corners=False))
+    return torch.stack(views, 1)
