@@ -60,6 +60,12 @@ def parse_args():
                         "top-k, this library and the reference's Triton kernel; aggregator: "
                         "config 3, the reference's VGGT aggregator end to end with its "
                         "Triton operator and with this drop-in")
+    p.add_argument("--qk-queries", type=int, default=0,
+                   help="qk-topk: query rows (default: all 43,808 tokens of the 32 frames)")
+    p.add_argument("--qk-topk", default="4,16,64",
+                   help="qk-topk: comma-separated top-k values per frame")
+    p.add_argument("--no-reference", action="store_true",
+                   help="qk-topk: skip the reference's Triton kernel")
     return p.parse_args()
 
 
@@ -540,9 +546,12 @@ def run_qk_topk_bench(args):
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
     g = torch.Generator(device=dev).manual_seed(0)
     frames, per, d = 32, 1369, 64
-    n = frames * per
+    nk = frames * per
+    n = args.qk_queries if args.qk_queries > 0 else nk
     q = torch.randn(1, n, d, device=dev, generator=g).to(torch.bfloat16)
-    k = torch.randn(1, n, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, nk, d, device=dev, generator=g).to(torch.bfloat16)
+    if args.no_reference:
+        ref = None
     peaks = load_peaks()
     peak = peaks.get("bf16_tflops") if peaks else None
 
@@ -561,15 +570,15 @@ def run_qk_topk_bench(args):
             ts.append(e0.elapsed_time(e1))
         return statistics.median(ts)
 
-    flops = 2.0 * n * n * d
-    for topk in (4, 16, 64):
+    flops = 2.0 * n * nk * d
+    for topk in (int(t) for t in args.qk_topk.split(",")):
         ours = lambda: vggt_sparse.compute_qk_topk_indices_fused(q, k, topk, num_toks_per_img=per)
         t_ms = timeit(ours)
         tf = flops / (t_ms * 1e-3) / 1e12
         line = {"component": "qk-topk", "unit": "ms",
                 "workload": "%d queries x %d keys (%d frames of %d), dim %d, top-%d per frame, bf16"
-                            % (n, n, frames, per, d, topk),
-                "ours_ms": t_ms, "scores_per_s": n * n / (t_ms * 1e-3),
+                            % (n, nk, frames, per, d, topk),
+                "ours_ms": t_ms, "scores_per_s": n * nk / (t_ms * 1e-3),
                 "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                              "frac": tf / peak if peak else None,
                              "note": "QK^T FLOPs 2*Nq*Nk*D over the call; of measured bf16 burst"},
