@@ -18,10 +18,14 @@
 //  * warps 2-5: selection, one query row per thread (TMEM lane = row).  A
 //    score passes if it is not below the row's current k-th best; passing
 //    scores are appended to a per-row candidate buffer with predicated
-//    shared-memory stores (no branch per score).  Every 32 columns the
-//    candidates are merged into the row's list: a sorted list in registers
-//    for topk <= 8, a min-heap in shared memory above.  After a frame's last
-//    tile the list is written out (in descending order) and reset.
+//    shared-memory stores (no branch per score), then merged into the row's
+//    list with every score checked exactly.  topk <= 8: a sorted list in
+//    registers, seeded with the frame's first four scores; scores are
+//    screened four at a time (a quad whose largest score passes is stored
+//    whole) and merged every 64 columns.  Above 8: a min-heap in shared
+//    memory; scores are screened one at a time and merged every 32 columns
+//    (with a large top-k most quads would pass).  After a frame's last tile
+//    the list is written out (in descending order) and reset.
 //
 // Every mbarrier wait is bounded (1 s); on expiry the CTA raises its abort
 // flag, records VGGT_STATUS_TIMEOUT, drains its in-flight copies, frees its
@@ -41,10 +45,12 @@ namespace qktopk {
 constexpr int BM = 128;                     // query rows per CTA
 constexpr int BN = 128;                     // keys per tile
 constexpr int THREADS = 192;
-constexpr int CHUNK = 32;                   // columns between merges
+constexpr int CHUNK = 64;                   // columns between merges (half a tile)
+constexpr int QUADS = CHUNK / 4;            // candidate slots: one 4-score quad each
 constexpr int MAX_STAGES = 4;
 constexpr uint32_t SPAN_BYTES = 128 * 128;  // 128 rows x 64 bf16: one 128-B swizzle span wide
-constexpr uint32_t CAND_BYTES = CHUNK * BM * 8;
+constexpr uint32_t CAND_STRIDE = BM * 16;   // one slot of every row: 16 bytes per row
+constexpr uint32_t CAND_BYTES = QUADS * CAND_STRIDE;
 constexpr uint32_t TMEM_COLS = 256;         // two S buffers of 128 columns
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
 
@@ -103,22 +109,66 @@ __device__ __forceinline__ float key2f(uint32_t key) {
   return __uint_as_float(key ^ (~(uint32_t)((int32_t)key >> 31) | 0x80000000u));
 }
 
-// Appends (score bits, key index) at `addr` and advances it by one candidate
-// row (BM * 8 bytes) when the score is not below `thr` (or either is NaN).
-__device__ __forceinline__ void screen(uint32_t& addr, uint32_t bits, float thr, uint32_t idx) {
+// Screens one quad of scores (columns 4Q .. 4Q+3 of a half tile): when the
+// largest is not below `thr` (or any of the five is NaN) the four score bits
+// are appended at `addr` (one 16-byte candidate slot), `addr` advances by one
+// slot and bit Q of `mask` is set.  No branch.
+template <int Q>
+__device__ __forceinline__ void screen_quad(uint32_t& addr, uint32_t& mask, const uint32_t (&s)[64],
+                                            float thr) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .f32 m;\n\t"
+      "max.NaN.f32 m, %2, %3, %4;\n\t"
+      "max.NaN.f32 m, m, %5;\n\t"
+      "setp.geu.f32 p, m, %6;\n\t"
+      "@p st.shared.v4.u32 [%0], {%7, %8, %9, %10};\n\t"
+      "@p add.u32 %0, %0, %12;\n\t"
+      "@p or.b32 %1, %1, %11;\n\t}"
+      : "+r"(addr), "+r"(mask)
+      : "f"(__uint_as_float(s[4 * Q])), "f"(__uint_as_float(s[4 * Q + 1])),
+        "f"(__uint_as_float(s[4 * Q + 2])), "f"(__uint_as_float(s[4 * Q + 3])), "f"(thr),
+        "r"(s[4 * Q]), "r"(s[4 * Q + 1]), "r"(s[4 * Q + 2]), "r"(s[4 * Q + 3]), "n"(1u << Q),
+        "n"(CAND_STRIDE)
+      : "memory");
+}
+
+// Quads Q .. QUADS-1 of a half tile; quads at or past column `lim` of the
+// half are skipped (lim >= 64: none).
+template <int Q>
+__device__ __forceinline__ void screen_quads(uint32_t& addr, uint32_t& mask, const uint32_t (&s)[64],
+                                             float thr, int lim) {
+  if constexpr (Q < QUADS) {
+    if (lim >= 64 || 4 * Q < lim) screen_quad<Q>(addr, mask, s, thr);
+    screen_quads<Q + 1>(addr, mask, s, thr, lim);
+  }
+}
+
+// The heap path screens score by score: with a large top-k most quads would
+// pass.  Appends (score bits, column) as one 8-byte slot when the score is
+// not below `thr` (or either is NaN) and advances `addr` by one slot.
+__device__ __forceinline__ void screen_one(uint32_t& addr, uint32_t bits, float thr, uint32_t col) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.geu.f32 p, %1, %2;\n\t"
       "@p st.shared.v2.u32 [%0], {%3, %4};\n\t"
-      "@p add.u32 %0, %0, 1024;\n\t}"
+      "@p add.u32 %0, %0, %5;\n\t}"
       : "+r"(addr)
-      : "f"(__uint_as_float(bits)), "f"(thr), "r"(bits), "r"(idx)
+      : "f"(__uint_as_float(bits)), "f"(thr), "r"(bits), "r"(col), "n"(BM * 8)
       : "memory");
 }
 
 __device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 
@@ -339,7 +389,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const int64_t qrow = qt * BM + row;
     const bool valid_row = qrow < p.n_queries;
-    const uint32_t cand_row = base + p.off_cand + (uint32_t)row * 8u;
+    const uint32_t cand_row = base + p.off_cand + (uint32_t)row * 16u;
     typename std::conditional<(KR > 0), RegList<(KR > 0 ? KR : 1)>, HeapList>::type list;
     if constexpr (KR == 0) {
       list.h = reinterpret_cast<unsigned long long*>(sbase + p.off_list);
@@ -351,14 +401,24 @@ __global__ void __launch_bounds__(THREADS, 2)
     float thr = __uint_as_float(0xffffffffu);  // NaN: every score passes
     bool ok = true;
 
-    auto merge = [&](uint32_t addr) {
-      const int cnt = (int)((addr - cand_row) >> 10);
+    // Inserts the half tile's passing quads in column order (an equal key
+    // then lands after the earlier, lower-index entry); every score of a
+    // quad is checked exactly against the list, columns >= lim skipped.
+    auto merge = [&](uint32_t addr, uint32_t mask, uint32_t col0, int lim) {
+      const int cnt = (int)((addr - cand_row) / CAND_STRIDE);
       const int mc = __reduce_max_sync(0xffffffffu, cnt);
       for (int c = 0; c < mc; ++c) {
         if (c < cnt) {
-          const uint2 e = ld_shared_v2(cand_row + (uint32_t)c * 1024u);
-          const uint32_t key = f2key(e.x);
-          if (key > list.last()) list.insert(key, e.y);
+          const int qd = __ffs(mask) - 1;
+          mask &= mask - 1u;
+          const uint4 e = ld_shared_v4(cand_row + (uint32_t)c * CAND_STRIDE);
+          const uint32_t v[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int col = 4 * qd + i;
+            const uint32_t key = f2key(v[i]);
+            if (col < lim && key > list.last()) list.insert(key, col0 + (uint32_t)col);
+          }
         }
       }
       thr = key2f(list.last());
@@ -381,7 +441,6 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tc_fence_after();
       const int64_t rem = p.tokens - (int64_t)j * BN;
       const int vc = rem < BN ? (int)rem : BN;  // valid columns of this tile
-      const uint32_t idx0 = (uint32_t)j * BN;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         uint32_t s[64];
@@ -393,22 +452,54 @@ __global__ void __launch_bounds__(THREADS, 2)
           tc::tc_fence_before();
           tc::mbar_arrive(bar(B_SEMPTY + buf));
         }
+        const int lim = vc - h * 64;  // valid columns of this half
+        if (lim <= 0) continue;       // uniform: the half is past the frame
+        const uint32_t col0 = (uint32_t)(j * BN + h * 64);
+        if constexpr (KR == 0) {
+          // heap: 32-column chunks of 8-byte (score, column) slots
+          const uint32_t row8 = base + p.off_cand + (uint32_t)row * 8u;
 #pragma unroll
-        for (int q4 = 0; q4 < 64 / CHUNK; ++q4) {
-          const int c0 = h * 64 + q4 * CHUNK;
-          if (c0 >= vc) break;  // uniform: the rest of the tile is past the frame
-          uint32_t addr = cand_row;
-          if (c0 + CHUNK <= vc) {
+          for (int c2 = 0; c2 < 2; ++c2) {
+            if (c2 * 32 >= lim) break;  // uniform
+            uint32_t addr = row8;
+            if (c2 * 32 + 32 <= lim) {
 #pragma unroll
-            for (int i = 0; i < CHUNK; ++i)
-              screen(addr, s[q4 * CHUNK + i], thr, idx0 + (uint32_t)(c0 + i));
-          } else {
+              for (int i = 0; i < 32; ++i) screen_one(addr, s[c2 * 32 + i], thr, col0 + c2 * 32 + i);
+            } else {
 #pragma unroll
-            for (int i = 0; i < CHUNK; ++i)
-              if (c0 + i < vc) screen(addr, s[q4 * CHUNK + i], thr, idx0 + (uint32_t)(c0 + i));
+              for (int i = 0; i < 32; ++i)
+                if (c2 * 32 + i < lim) screen_one(addr, s[c2 * 32 + i], thr, col0 + c2 * 32 + i);
+            }
+            const int cnt = (int)((addr - row8) / (BM * 8));
+            const int mc = __reduce_max_sync(0xffffffffu, cnt);
+            for (int c = 0; c < mc; ++c) {
+              if (c < cnt) {
+                const uint2 e = ld_shared_v2(row8 + (uint32_t)c * (BM * 8));
+                const uint32_t key = f2key(e.x);
+                if (key > list.last()) list.insert(key, e.y);
+              }
+            }
+            thr = key2f(list.last());
           }
-          merge(addr);
+          continue;
         }
+        uint32_t addr = cand_row, mask = 0u;
+        {
+          if (j == 0 && h == 0) {
+            // the frame's first quad goes straight into the empty list, so
+            // the screen starts with a real k-th best
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t key = f2key(s[i]);
+              if (i < lim && key > list.last()) list.insert(key, (uint32_t)i);
+            }
+            thr = key2f(list.last());
+            screen_quads<1>(addr, mask, s, thr, lim);
+          } else {
+            screen_quads<0>(addr, mask, s, thr, lim);
+          }
+        }
+        merge(addr, mask, col0, lim);
       }
       if (j == tpf - 1 && valid_row)
         list.write(out_row + f * p.topk, p.topk, (int32_t)(f * p.tokens));
