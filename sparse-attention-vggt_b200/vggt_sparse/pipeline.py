@@ -31,6 +31,9 @@ class HostPipeline:
     def _buffers(self, k, host):
         bufs = self._sets[k]
         if bufs is None or any(b.shape != h.shape or b.dtype != h.dtype for b, h in zip(bufs, host)):
+            if self._free[k] is not None:
+                # the old set may still be read by its call's compute or download
+                self._free[k].synchronize()
             dev = torch.device("cuda", torch.cuda.current_device())
             bufs = [torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host]
             self._sets[k] = bufs

@@ -46,6 +46,7 @@ SHAPES = [
     (1, 40, 1, 1000, 64, 128),   # the largest top-k
     (1, 48, 3, 90, 32, 6),       # head dim 32 (zero-padded to 64)
     (1, 33, 4, 129, 96, 9),      # head dim 96 (zero-padded to 128), 9 -> shared list
+    (1, 130, 2, 400, 128, 100),  # head dim 128 with a 100-entry heap: a single K stage
 ]
 
 

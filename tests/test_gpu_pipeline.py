@@ -38,3 +38,19 @@ def test_pipeline_reuses_one_output_buffer_in_order(cuda):
     pipe.synchronize()
     last = layers[-1]
     assert torch.equal(out, layer(last.q, last.kp, last.vp, last.ks, last.vs).cpu())
+
+
+def test_pipeline_follows_a_change_of_shape(cuda):
+    small = clustered_layer(2, centres=32, seed=50, device=cuda)
+    big = clustered_layer(4, centres=32, seed=51, device=cuda)
+    layer = vggt_sparse.SparseGlobalLayer(16, mode="topk", retention=0.25, kernel="tcgen05")
+    pipe = vggt_sparse.HostPipeline(layer)
+    outs = []
+    for x in (small, big, small, big):
+        h = [t.cpu().pin_memory() for t in (x.q, x.kp, x.vp, x.ks, x.vs)]
+        o = torch.empty(x.q.shape, dtype=x.q.dtype).pin_memory()
+        pipe(*h, out=o)
+        outs.append((x, o))
+    pipe.synchronize()
+    for x, o in outs:
+        assert torch.equal(o, layer(x.q, x.kp, x.vp, x.ks, x.vs).cpu())
