@@ -28,6 +28,7 @@
 #ifndef VGGT_SPARSE_H
 #define VGGT_SPARSE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus

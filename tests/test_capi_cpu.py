@@ -33,6 +33,21 @@ def test_header_declares_the_documented_entry_points():
         "vggt_sparse_version", "vggt_token_sparse_attention"])
 
 
+@pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++17")])
+def test_header_compiles_alone(lang, std, tmp_path):
+    """include/vggt_sparse.h is self-contained plain C (a cgo / ctypes-style
+    caller includes it with nothing before it)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc" if lang == "c" else "g++")
+    if cc is None:
+        pytest.skip("no host compiler")
+    hdr = os.path.join(REPO, "include", "vggt_sparse.h")
+    res = subprocess.run([cc, "-fsyntax-only", "-x", lang, std, "-Wall", "-Wextra", "-pedantic",
+                          "-Werror", hdr], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
 def test_library_exports_every_declared_symbol(lib):
     from vggt_sparse import _lib
     for name in declared_symbols():
