@@ -67,16 +67,20 @@ __global__ void __launch_bounds__(WARPS * 32)
   const int64_t r = (int64_t)blockIdx.x * WARPS + warp;
   if (r >= n_queries) return;
 
-  // the query row, fp32, in every lane
-  float qf[D];
+  // the query row, fp32, in shared memory: every lane reads it with
+  // broadcast 16-byte loads during its dot product (registers stay free for
+  // more warps in flight, which this gather needs)
+  __shared__ __align__(16) float qs[WARPS][D];
   {
-    const uint4* src = reinterpret_cast<const uint4*>(q + r * D);
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 raw = __ldg(src + c);
-      unpack<T, 8>(raw, qf + 8 * c);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(q + r * D);
+    for (int e = lane; e < D / 2; e += 32) {
+      const float2 f = ElemOps<T>::to_float2(src[e]);
+      qs[warp][2 * e] = f.x;
+      qs[warp][2 * e + 1] = f.y;
     }
+    __syncwarp();
   }
+  const float4* q4 = reinterpret_cast<const float4*>(qs[warp]);
   const int half = lane >> 4;     // which key of a pair this half-warp takes
   const int dim0 = (lane & 15) * PD;
   float acc[PD];
@@ -90,10 +94,13 @@ __global__ void __launch_bounds__(WARPS * 32)
   // dims up to 64, 4 at a time for 128 (register budget)
   constexpr int G = D <= 64 ? 16 : 4;
   using VT = typename Vec<PD>::type;
+  // each chunk's key index is loaded one chunk ahead
+  int32_t kb_next = lane < topk ? irow[lane] : -1;
   for (int64_t c = 0; c < topk; c += 32) {
     const int64_t j = c + lane;
     const bool in_range = j < topk;
-    const int32_t kb = in_range ? irow[j] : -1;
+    const int32_t kb = in_range ? kb_next : -1;
+    if (j + 32 < topk) kb_next = irow[j + 32];
     const bool ok = in_range && kb >= 0 && kb < n_keys;
     bad |= in_range && !ok;
     // every gather of the chunk is issued before any of it is used: this
@@ -122,8 +129,10 @@ __global__ void __launch_bounds__(WARPS * 32)
     for (int cc = 0; cc < D / 8; ++cc) {
       float kf[8];
       unpack<T, 8>(kraw[cc], kf);
+      const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) dot = fmaf(qf[8 * cc + e], kf[e], dot);
+      for (int e = 0; e < 8; ++e) dot = fmaf(qv[e], kf[e], dot);
     }
     const float s = ok ? dot * scale_log2 : -INFINITY;
     float cmax = s;
