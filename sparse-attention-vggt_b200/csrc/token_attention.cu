@@ -9,8 +9,9 @@
 //
 // One warp per query, keys in chunks of 32 with an online softmax in the exp2
 // domain:
-//   * scores: lane j gathers key idx[c + j] (one D-element row, 16-byte loads)
-//     and dots it with the query row held in registers;
+//   * scores: the chunk's K rows are gathered coalesced (D/8 lanes per row, a
+//     16-byte segment each), dotted segment-wise with the query, summed across
+//     the row's lanes, and key idx[c + j]'s score is moved to lane j;
 //   * P.V: each half-warp takes one key at a time, its 16 lanes holding D/16
 //     dims each, so every gathered V row is read as one coalesced segment;
 //     the two halves' sums combine at the end.
@@ -56,7 +57,7 @@ __device__ __forceinline__ void unpack(const typename Vec<N>::type& raw, float* 
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, 4)
     token_attn_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                       const int32_t* __restrict__ idx, int64_t idx_stride, int64_t n_queries,
                       int64_t n_keys, int64_t topk, float scale_log2, T* __restrict__ out,
@@ -67,20 +68,18 @@ __global__ void __launch_bounds__(WARPS * 32)
   const int64_t r = (int64_t)blockIdx.x * WARPS + warp;
   if (r >= n_queries) return;
 
-  // the query row, fp32, in shared memory: every lane reads it with
-  // broadcast 16-byte loads during its dot product (registers stay free for
-  // more warps in flight, which this gather needs)
-  __shared__ __align__(16) float qs[WARPS][D];
+  // K rows are read whole and coalesced: SEG lanes share a row, each holding
+  // one 16-byte segment (8 elements), so one load instruction covers RPI rows
+  // (a lane reading a whole row by itself costs an L1 wavefront per row per
+  // instruction, which bounded the gather).  Each lane keeps its segment of
+  // the query row, fp32.
+  constexpr int SEG = D / 8, RPI = 32 / SEG;
+  const int grp = lane / SEG, seg = lane % SEG;
+  float q8[8];
   {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(q + r * D);
-    for (int e = lane; e < D / 2; e += 32) {
-      const float2 f = ElemOps<T>::to_float2(src[e]);
-      qs[warp][2 * e] = f.x;
-      qs[warp][2 * e + 1] = f.y;
-    }
-    __syncwarp();
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(q + r * D) + seg);
+    unpack<T, 8>(raw, q8);
   }
-  const float4* q4 = reinterpret_cast<const float4*>(qs[warp]);
   const int half = lane >> 4;     // which key of a pair this half-warp takes
   const int dim0 = (lane & 15) * PD;
   float acc[PD];
@@ -104,12 +103,15 @@ __global__ void __launch_bounds__(WARPS * 32)
     const bool ok = in_range && kb >= 0 && kb < n_keys;
     bad |= in_range && !ok;
     // every gather of the chunk is issued before any of it is used: this
-    // lane's K row, then the first group of V slices of its half-warp's keys
-    uint4 kraw[D / 8];
-    {
-      const uint4* kr = reinterpret_cast<const uint4*>(k + (int64_t)(ok ? kb : 0) * D);
+    // lane's segment of keys RPI*i + grp (i < SEG), then the first group of
+    // V slices of its half-warp's keys
+    uint4 kraw[SEG];
 #pragma unroll
-      for (int cc = 0; cc < D / 8; ++cc) kraw[cc] = __ldg(kr + cc);
+    for (int i = 0; i < SEG; ++i) {
+      const int src = RPI * i + grp;
+      const int32_t ki = __shfl_sync(full, kb, src);
+      const bool oki = c + src < topk && ki >= 0 && ki < n_keys;
+      kraw[i] = __ldg(reinterpret_cast<const uint4*>(k + (int64_t)(oki ? ki : 0) * D) + seg);
     }
     VT vraw[G];
     bool vok[G];
@@ -124,15 +126,25 @@ __global__ void __launch_bounds__(WARPS * 32)
       }
     };
     fetch_v(0);
+    // partial dot products over each segment, summed across the SEG lanes
+    // of a row, then key j's score moved to lane j
+    float part[SEG];
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      float kf[8];
+      unpack<T, 8>(kraw[i], kf);
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d = fmaf(q8[e], kf[e], d);
+#pragma unroll
+      for (int off = 1; off < SEG; off <<= 1) d += __shfl_xor_sync(full, d, off);
+      part[i] = d;
+    }
     float dot = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < D / 8; ++cc) {
-      float kf[8];
-      unpack<T, 8>(kraw[cc], kf);
-      const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
-      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) dot = fmaf(qv[e], kf[e], dot);
+    for (int i = 0; i < SEG; ++i) {
+      const float d = __shfl_sync(full, part[i], (lane % RPI) * SEG);
+      if (lane / RPI == i) dot = d;
     }
     const float s = ok ? dot * scale_log2 : -INFINITY;
     float cmax = s;
