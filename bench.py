@@ -255,14 +255,22 @@ def shard_inputs(x, cfg, rank, world, shard, device):
     return (*sel, dense, (0, x.shape.n_tokens))
 
 
-def cpu_baseline(cfg, x_cpu, sample_blocks):
+def _spread_blocks(qbc, n):
+    n = min(n, qbc)
+    return sorted(set(int(round(i * (qbc - 1) / max(n - 1, 1))) for i in range(n)))
+
+
+def cpu_baseline(cfg, x_cpu, sample_blocks, check_blocks=None):
     """The reference's CPU PyTorch path (restated in oracle.cpu_path) on a
-    bounded sample of query blocks, extrapolated to ms per full layer."""
+    bounded sample of query blocks spread over the layer, extrapolated to ms
+    per full layer: pooling over the whole layer (timed once) plus the
+    sample's per-query-block cost times the layer's query blocks.  With
+    ``check_blocks`` a second, smaller sample is timed too and both per-block
+    costs are reported, so the extrapolation's dependence on the sample size
+    is visible."""
     from oracle import cpu_path
     shape = x_cpu.shape
     qbc = shape.n_qblocks
-    nsample = min(sample_blocks, qbc)
-    qblocks = sorted(set(int(round(i * (qbc - 1) / max(nsample - 1, 1))) for i in range(nsample)))
     scale = cfg.dim ** -0.5
     if cfg.mode == "topk":
         from oracle import topk_budget
@@ -270,22 +278,35 @@ def cpu_baseline(cfg, x_cpu, sample_blocks):
                              cfg.block)
     else:
         budget = cfg.tau
-    q, kp, vp, ks, vs = (t.float() for t in (x_cpu.q, x_cpu.kp, x_cpu.vp, x_cpu.ks, x_cpu.vs))
+    q, kp, vp, ks, vs, k, v = (t.float() for t in (x_cpu.q, x_cpu.kp, x_cpu.vp, x_cpu.ks,
+                                                     x_cpu.vs, x_cpu.k, x_cpu.v))
     t0 = time.perf_counter()
     cpu_path.block_mean(q, cfg.block)
     cpu_path.block_mean(kp, cfg.block)
     t_pool = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    cpu_path.layer_sample(q, kp, vp, ks, vs, mode=cfg.mode, budget=budget,
-                          dense_heads=cfg.dense_heads, qblocks=qblocks, scale=scale,
-                          block=cfg.block)
-    t_sample = time.perf_counter() - t0
-    per_block = max(t_sample - t_pool, 0.0) / len(qblocks)
-    ms = (t_pool + per_block * qbc) * 1e3
-    return {"value": ms, "unit": "ms/layer", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": "%d of %d query blocks x 16 heads of %s (estimator pooling over the full "
-                      "layer), torch fp32 CPU, extrapolated linearly; %.1f s measured"
-                      % (len(qblocks), qbc, cfg.name, t_pool + t_sample)}
+
+    def per_block(n):
+        qblocks = _spread_blocks(qbc, n)
+        t0 = time.perf_counter()
+        cpu_path.layer_sample(q, kp, vp, ks, vs, mode=cfg.mode, budget=budget,
+                              dense_heads=cfg.dense_heads, qblocks=qblocks, scale=scale,
+                              block=cfg.block, k_full=k, v_full=v)
+        t = time.perf_counter() - t0
+        # the sample re-pools the layer; that part is counted once, in t_pool
+        return max(t - t_pool, 0.0) / len(qblocks), len(qblocks), t
+
+    pb, n, t_sample = per_block(sample_blocks)
+    ms = (t_pool + pb * qbc) * 1e3
+    out = {"value": ms, "unit": "ms/layer", "cores": torch.get_num_threads(), "kind": "port",
+           "extrapolated": True, "per_qblock_ms": pb * 1e3, "sample_qblocks": n,
+           "sample": "%d of %d query blocks x 16 heads of %s (estimator pooling over the full "
+                     "layer), torch fp32 CPU, extrapolated linearly to all query blocks; %.1f s "
+                     "measured" % (n, qbc, cfg.name, t_pool + t_sample)}
+    if check_blocks:
+        pb2, n2, _ = per_block(check_blocks)
+        out["per_qblock_ms_check"] = {"sample_qblocks": n2, "per_qblock_ms": pb2 * 1e3,
+                                      "ratio_to_main": pb2 / pb if pb > 0 else None}
+    return out
 
 
 def workload_desc(cfg, shape):
@@ -307,17 +328,25 @@ def run_reference_arm(args, rank, world):
     x = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device="cpu",
                         dtype=torch.bfloat16)
     torch.set_num_threads(os.cpu_count() or 1)
-    sample = max(4, args.cpu_sample_blocks // 4)
+    # the same query-block sample as the cpu_baseline leg of the GPU arm
     for _ in range(args.warmup):
         cpu_baseline(cfg, x, 2)
-    vals = [cpu_baseline(cfg, x, sample) for _ in range(args.steps)]
+    vals = [cpu_baseline(cfg, x, args.cpu_sample_blocks) for _ in range(args.steps)]
     ms = statistics.median(v["value"] for v in vals)
     cb = dict(vals[0])
     cb["value"] = ms
+    cb["per_qblock_ms"] = statistics.median(v["per_qblock_ms"] for v in vals)
+    cb["per_qblock_ms_spread"] = [min(v["per_qblock_ms"] for v in vals),
+                                  max(v["per_qblock_ms"] for v in vals)]
     line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "extrapolated": True,
+            "note": "each step times the reference's CPU path on %d query blocks spread over "
+                    "the layer and extrapolates linearly to the full layer; value is the median "
+                    "of the steps' extrapolations, not a measured full-layer step"
+                    % cb["sample_qblocks"],
             "config": {"workload": workload_desc(cfg, x.shape), "frames": cfg.frames,
                        "tokens": x.shape.n_tokens, "heads": 16, "head_dim": 64},
             "cpu_baseline": cb,
@@ -844,7 +873,8 @@ def main():
         launches_per_step += 4
         items = n_slots * ((-(-q.shape[1] // cfg.block) + 1) // 2)
         forced = os.environ.get("VGGT_ATTN_SPLIT", "")
-        split = int(forced) if forced in ("1", "2", "3", "4") else (2 if items < 4 * 296 else 1)
+        wave = 2 * torch.cuda.get_device_properties(device).multi_processor_count
+        split = int(forced) if forced in ("1", "2", "3", "4") else (2 if items < 4 * wave else 1)
         if split > 1:
             launches_per_step += 1
 
@@ -926,7 +956,7 @@ def main():
         host_out = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
         h2d = sum(t.numel() * t.element_size() for t in host)
         d2h = host_out[0].numel() * host_out[0].element_size()
-        e2e_steps = max(3, args.steps // 5)
+        e2e_steps = args.steps
 
         def serial_step():
             for d_, h_ in zip(dev_in, host):
@@ -973,7 +1003,8 @@ def main():
         x_cpu = clustered_layer(cfg.frames, centres=cfg.centres, seed=0, device="cpu",
                                 dtype=torch.bfloat16)
         torch.set_num_threads(os.cpu_count() or 1)
-        cpu = cpu_baseline(cfg, x_cpu, args.cpu_sample_blocks)
+        cpu = cpu_baseline(cfg, x_cpu, args.cpu_sample_blocks,
+                           check_blocks=max(2, args.cpu_sample_blocks // 2))
 
     if rank != 0:
         if world > 1:
@@ -1011,7 +1042,10 @@ def main():
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": att_tflops / peaks["bf16_tflops"],
                      "traffic": profiled_traffic(args.config),
-                     "traffic_unit": "bytes per launch (dram read + write, from profiles/)",
+                     "traffic_unit": "bytes per launch (dram read + write)",
+                     "traffic_source": "static: the committed ncu capture "
+                                       "profiles/attn_tc05_%s.md of this workload, not "
+                                       "measured in this run" % args.config,
                      "flops_per_launch": flops_local,
                      "peak_source": peaks["source"] + " bf16 burst"},
         "estimator_roofline": {"bound": "hbm", "achieved": est_bytes / (est_local * 1e-3) / 1e9,

@@ -253,6 +253,10 @@ int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int6
  * exceeds 8 MiB (e.g. 16 heads x 43,968 tokens x 64 dims needs 5.6 MiB).
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  The address is cached per device together
+ * with the CUDA context it belongs to; after cudaDeviceReset (or when the
+ * primary context is released and created again) the next call sees a new
+ * context and looks the address up again, so that call should also come
  * before any stream capture.  All calls share the one array: calls whose
  * work can overlap on the GPU (other streams, other threads) race on it and
  * must be serialised by the caller.

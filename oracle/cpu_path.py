@@ -52,16 +52,24 @@ def estimate(q, kp, mode, budget, scale, block=64, qblocks=None):
 
 
 def sparse_layer(q, kp, vp, ks, vs, ids, counts, sparse_heads, dense_heads, qblocks, scale,
-                 block=64):
-    """Attention output rows of the sampled query blocks, [H, rows, d]."""
+                 block=64, k_full=None, v_full=None):
+    """Attention output rows of the sampled query blocks, [H, rows, d].
+
+    Dense heads attend over the layer's full k/v [H, N, d], which the
+    reference's dense branch reads as they are (``k_full``/``v_full``); when
+    they are not given, patch and special keys are concatenated here."""
     h, n, d = q.shape
     npatch = kp.shape[1]
     rows = [torch.arange(b * block, min((b + 1) * block, n)) for b in qblocks]
     out = torch.empty((h, sum(len(r) for r in rows), d))
     k_all = v_all = None
     if dense_heads:
-        k_all = torch.cat((kp, ks), 1).float()
-        v_all = torch.cat((vp, vs), 1).float()
+        hh = torch.tensor(dense_heads)
+        if k_full is not None and v_full is not None:
+            k_all, v_all = k_full[hh].float(), v_full[hh].float()
+        else:
+            k_all = torch.cat((kp[hh], ks[hh]), 1).float()
+            v_all = torch.cat((vp[hh], vs[hh]), 1).float()
     for head in sparse_heads:
         off = 0
         for j, b in enumerate(qblocks):
@@ -76,17 +84,17 @@ def sparse_layer(q, kp, vp, ks, vs, ids, counts, sparse_heads, dense_heads, qblo
             off += len(qr)
     if dense_heads:
         qr = torch.cat(rows)
-        hh = torch.tensor(dense_heads)
-        out[hh] = F.scaled_dot_product_attention(q[hh][:, qr].float()[None], k_all[hh][None],
-                                                 v_all[hh][None], scale=scale)[0]
+        out[hh] = F.scaled_dot_product_attention(q[hh][:, qr].float()[None], k_all[None],
+                                                 v_all[None], scale=scale)[0]
     return out
 
 
-def layer_sample(q, kp, vp, ks, vs, *, mode, budget, dense_heads, qblocks, scale, block=64):
+def layer_sample(q, kp, vp, ks, vs, *, mode, budget, dense_heads, qblocks, scale, block=64,
+                 k_full=None, v_full=None):
     """Estimator (pooling over the full layer, scores/selection for the
     sampled query blocks) + attention for the sampled query blocks."""
     h = q.shape[0]
     sparse = [x for x in range(h) if x not in set(dense_heads)]
     ids, counts = estimate(q, kp, mode, budget, scale, block, qblocks)
     return sparse_layer(q, kp, vp, ks, vs, ids, counts, sparse, list(dense_heads), qblocks,
-                        scale, block)
+                        scale, block, k_full=k_full, v_full=v_full)

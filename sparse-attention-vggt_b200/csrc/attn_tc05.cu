@@ -898,10 +898,10 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-int64_t attn_tc05_split(int64_t items) {
-  // grids of fewer than 4 waves (2 CTAs on each of 148 SMs) are split toward
-  // 8 waves, at most 4 ways; longer grids keep one CTA per item
-  constexpr int64_t kWave = 2 * 148;
+int64_t attn_tc05_split(int64_t items, int sms) {
+  // grids of fewer than 4 waves (2 CTAs on each SM) are split toward 8
+  // waves, at most 4 ways; longer grids keep one CTA per item
+  const int64_t kWave = 2 * (int64_t)(sms > 0 ? sms : 148);
   if (items <= 0 || items >= 4 * kWave) return 1;
   const int64_t s = (8 * kWave + items - 1) / items;
   return s > 4 ? 4 : s;

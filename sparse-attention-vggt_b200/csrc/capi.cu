@@ -4,6 +4,8 @@
 // for unsupported dtypes (saf3r/triton/adaptive_block_attention.py:72-73):
 // here every argument error returns a negative code and leaves a message in
 // vggt_sparse_last_error(); nothing is launched in that case.
+#include <cuda.h>
+
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -36,14 +38,24 @@ int cuda_rc(cudaError_t e) {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Multiprocessors of the current device (0 when it cannot be queried).
+int current_device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  return sms;
+}
+
 // Splits per work item of the tcgen05 kernel: VGGT_ATTN_SPLIT (1-4) when set,
-// else enough for about 8 waves of CTAs (1 for large grids).
+// else enough for about 8 waves of CTAs on the current device (1 for large
+// grids).
 int64_t attention_split(int64_t items) {
   if (const char* env = std::getenv("VGGT_ATTN_SPLIT")) {
     const long v = std::strtol(env, nullptr, 10);
     if (v >= 1 && v <= 4) return v;
   }
-  return vggt::attn_tc05_split(items);
+  return vggt::attn_tc05_split(items, current_device_sms());
 }
 
 }  // namespace
@@ -200,7 +212,10 @@ int vggt_token_sparse_attention(const void* q, const void* k, const void* v,
     return fail("negative size argument");
   if (!std::isfinite(scale)) return fail("scale must be finite");
   if (n_queries == 0) return 0;
-  if (n_queries > (int64_t)0x7fffffff * 8) return fail("too many queries");
+  // one CTA per vggt::kTokenAttnQueriesPerCta queries; the grid's x extent is at most 2^31 - 1
+  if (n_queries > (int64_t)0x7fffffff * vggt::kTokenAttnQueriesPerCta)
+    return fail("too many queries (at most %lld)",
+                (long long)0x7fffffff * vggt::kTokenAttnQueriesPerCta);
   if (!q || !k || !v || !out || (topk > 0 && !indices))
     return fail("q, k, v, out and indices must be non-NULL");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
@@ -393,25 +408,58 @@ constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB of fp32 pooled rows
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 constexpr int kMaxDevices = 64;
-float* g_noalloc_ptr[kMaxDevices] = {};  // device address of the array, per device
+// Device address of the array per device ordinal, with the context it was
+// looked up in: a device reset (or a released and re-created primary context)
+// gives the array a new address, so a cached address is reused only while the
+// same context is current.
+struct NoallocCache {
+  void* ctx;
+  float* ptr;
+};
+NoallocCache g_noalloc_cache[kMaxDevices] = {};
 std::mutex g_noalloc_mutex;
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
 
 // Device address of the scratch array on the current device.  The host-side
 // name g_noalloc_scratch is only a stand-in for the symbol, never a device
-// pointer, so the address is looked up once per device and cached.
+// pointer, so the address is looked up with cudaGetSymbolAddress (with the
+// device current) the first time a context uses it, then cached.
 int noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_rc(e);
   if (dev < 0 || dev >= kMaxDevices) return fail("device ordinal %d not supported", dev);
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (get == nullptr) return fail("cuCtxGetCurrent is unavailable from the driver");
+  CUcontext ctx = nullptr;  // stays null before the thread's first CUDA call
+  if (get(&ctx) != CUDA_SUCCESS) return fail("cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  NoallocCache& c = g_noalloc_cache[dev];
+  if (ctx == nullptr || c.ptr == nullptr || c.ctx != static_cast<void*>(ctx)) {
     void* ptr = nullptr;
+    // also makes the device's primary context current when none was
     e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_rc(e);
-    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    if (get(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return fail("no current CUDA context on device %d", dev);
+    c.ctx = static_cast<void*>(ctx);
+    c.ptr = static_cast<float*>(ptr);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = c.ptr;
   return 0;
 }
 

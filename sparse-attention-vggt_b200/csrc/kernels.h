@@ -89,6 +89,8 @@ struct TokenAttnArgs {
   int32_t* status;
 };
 cudaError_t launch_token_attention(const TokenAttnArgs& a, cudaStream_t stream);
+// queries handled by one CTA of the per-token kernel (one warp each)
+constexpr int kTokenAttnQueriesPerCta = 4;
 
 // frame_topk.cu: per-frame QK top-k
 struct FrameTopkArgs {
@@ -108,9 +110,10 @@ cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu
 bool attn_tc05_supported(const AttnArgs& a);
 cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream);
-// splits per work item for a grid of `items` 128-row work items, and the
-// scratch bytes the split needs (0 when nsplit <= 1)
-int64_t attn_tc05_split(int64_t items);
+// splits per work item for a grid of `items` 128-row work items on a device
+// with `sms` multiprocessors, and the scratch bytes the split needs (0 when
+// nsplit <= 1)
+int64_t attn_tc05_split(int64_t items, int sms);
 size_t attn_tc05_split_bytes(int64_t items, int64_t nsplit);
 
 }  // namespace vggt

@@ -28,7 +28,7 @@ namespace vggt {
 
 namespace tokattn {
 
-constexpr int WARPS = 4;  // queries per CTA (3 CTAs per SM at dim 64)
+constexpr int WARPS = kTokenAttnQueriesPerCta;  // queries per CTA (3 CTAs per SM at dim 64)
 
 template <int N>
 struct Vec;  // N bf16/fp16 values as one load

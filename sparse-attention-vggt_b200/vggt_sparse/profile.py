@@ -14,8 +14,11 @@ import json
 DENSE_MODES = ("full", "dense")
 
 
-def dense_heads_from_profile(profile, layer, num_heads):
-    """Dense head ids of ``layer`` from a profile dict or JSON path."""
+def head_modes_from_profile(profile, layer, num_heads):
+    """The mode of each head of ``layer`` ("full" when no group lists it) from
+    a profile dict or JSON path, as saf3r/patch/wrapper.py:29-40 assigns
+    them; a head listed by two groups raises ValueError.  The profile is not
+    modified."""
     if isinstance(profile, str):
         with open(profile) as f:
             profile = json.load(f)
@@ -27,6 +30,12 @@ def dense_heads_from_profile(profile, layer, num_heads):
             if modes[head] != "full":
                 raise ValueError("Head %d assigned to multiple patterns!" % head)
             modes[head] = group["mode"]
+    return modes
+
+
+def dense_heads_from_profile(profile, layer, num_heads):
+    """Dense head ids of ``layer`` from a profile dict or JSON path."""
+    modes = head_modes_from_profile(profile, layer, num_heads)
     return [h for h, m in enumerate(modes) if m in DENSE_MODES]
 
 

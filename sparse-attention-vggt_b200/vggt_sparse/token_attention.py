@@ -12,7 +12,6 @@ from .ops import _ptr, _require_cuda, _stream, dtype_code
 
 
 def token_sparse_attention(q, k, v, kv_indices, scale=None, *, out=None, status=None):
-    _require_cuda(q, k, v, kv_indices, out, status)
     if q.dim() != 2 or k.dim() != 2 or v.dim() != 2 or kv_indices.dim() != 2:
         raise ValueError("q [N, D], k [Nk, D], v [Nk, D] and kv_indices [N, TopK] expected")
     n, d = q.shape
@@ -33,6 +32,13 @@ def token_sparse_attention(q, k, v, kv_indices, scale=None, *, out=None, status=
         idx = idx.contiguous()
     if out is None:
         out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
+        # the kernel writes N * D elements of q's dtype, row by row, from out's first byte
+        raise ValueError("out must be a contiguous %s tensor of shape %s"
+                         % (q.dtype, tuple(q.shape)))
+    if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
+        raise ValueError("status must be an int32 tensor with at least one element")
+    _require_cuda(q, k, v, kv_indices, out, status)
     scale = d ** -0.5 if scale is None else float(scale)
     lib = _lib.load()
     rc = lib.vggt_token_sparse_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(idx), idx.stride(0), n,

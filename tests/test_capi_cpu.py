@@ -164,6 +164,35 @@ def test_token_attention_argument_errors(lib):
     assert call(n=0) == 0
 
 
+def test_token_attention_checks_out_and_status():
+    """A caller's out must have q's shape and dtype and be contiguous, and status
+    must be int32: the kernel writes N * D elements of q's dtype from out's first
+    byte.  These checks run before any device work, so CPU tensors reach them."""
+    import torch
+    import vggt_sparse
+    q = torch.zeros(8, 64, dtype=torch.bfloat16)
+    kv = torch.zeros(20, 64, dtype=torch.bfloat16)
+    idx = torch.zeros(8, 4, dtype=torch.int32)
+    for bad in (torch.empty(4, 64, dtype=torch.bfloat16),              # too small
+                torch.empty(8, 64, dtype=torch.float32),               # other dtype
+                torch.empty(64, 8, dtype=torch.bfloat16).t()):         # not contiguous
+        with pytest.raises(ValueError, match="out must be"):
+            vggt_sparse.token_sparse_attention(q, kv, kv, idx, out=bad)
+    for bad in (torch.zeros(1, dtype=torch.int64), torch.zeros(0, dtype=torch.int32)):
+        with pytest.raises(ValueError, match="status must be"):
+            vggt_sparse.token_sparse_attention(q, kv, kv, idx, status=bad)
+    with pytest.raises(ValueError, match="CUDA"):  # well-formed CPU call: no CPU path
+        vggt_sparse.token_sparse_attention(q, kv, kv, idx, out=torch.empty_like(q))
+
+
+def test_token_attention_query_limit(lib):
+    lim = 0x7fffffff * 4  # the grid has one CTA per 4 queries, at most 2^31 - 1 CTAs
+    call = lambda n: lib.vggt_token_sparse_attention(16, 16, 16, 16, 4, n, 100, 4, 64, 0,
+                                                     0.125, 16, None, None)
+    assert call(lim + 1) < 0
+    assert "too many queries" in lib.vggt_sparse_last_error().decode()
+
+
 def test_frame_topk_argument_errors(lib):
     call = lambda **kw: lib.vggt_frame_qk_topk(*dict(dict(
         q=16, k=16, out=16, batch=1, nq=8, frames=2, tokens=100, dim=64, topk=4, groups=0,

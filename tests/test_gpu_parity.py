@@ -37,6 +37,22 @@ def check_out(actual, expected, rtol=0.02, atol=0.006):
     assert np.mean(np.abs(a - e)) / max(np.mean(np.abs(e)), 1e-12) <= 1e-2
 
 
+@pytest.mark.parametrize("cfg,tau", [("cfg2", 0.9), ("cfg5", 0.85)])
+def test_mass_select_on_layer_rows_matches_reference_counts(cuda, golden, cfg, tau):
+    """The kernel's mass selection on pooled-score rows of the 32- and
+    256-frame layers (tests/golden/mass_rows.npz): ids bit-exact against the
+    oracle and counts equal to the reference's own fp32 softmax +
+    concentration rule recorded in the fixture."""
+    g = golden("mass_rows.npz")
+    scores = g["%s_scores" % cfg]
+    ids, counts = vggt_sparse.block_select(torch.tensor(scores, device=cuda), mode="mass",
+                                           tau=tau)
+    exp, exp_counts = oracle.select_mass(scores, tau)
+    np.testing.assert_array_equal(counts.cpu().numpy(), exp_counts)
+    np.testing.assert_array_equal(ids.cpu().numpy(), exp)
+    np.testing.assert_array_equal(counts.cpu().numpy(), g["%s_m%d" % (cfg, round(tau * 100))])
+
+
 @pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("case", ["d64_bq64_bk64", "d32_bq32_bk128", "d64_bq32_bk32",
@@ -260,16 +276,50 @@ def test_invalid_ids_counts_heads_raise(cuda):
     bad_id = torch.tensor([[[0, 7]]], device=cuda, dtype=torch.int32)
     two = torch.tensor([2], device=cuda, dtype=torch.int32)
     with pytest.raises(ValueError, match="block id"):
-        vggt_sparse.block_attention(q, kp, kp, ks, ks, bad_id, two, heads)
+        vggt_sparse.block_attention(q, kp, kp, ks, ks, bad_id, two, heads, validate=True)
     with pytest.raises(ValueError, match="count"):
         vggt_sparse.block_attention(q, kp, kp, ks, ks, bad_id, torch.tensor(
-            [5], device=cuda, dtype=torch.int32), heads)
+            [5], device=cuda, dtype=torch.int32), heads, validate=True)
     with pytest.raises(ValueError, match="head id"):
         vggt_sparse.block_attention(q, kp, kp, ks, ks, bad_id[:, :, :1], two.clamp(max=1),
-                                    torch.tensor([4], device=cuda, dtype=torch.int32))
+                                    torch.tensor([4], device=cuda, dtype=torch.int32),
+                                    validate=True)
     # the context is still usable afterwards
     torch.cuda.synchronize()
     assert torch.isfinite(q.float()).all()
+
+
+def test_default_validation_is_deferred_and_never_syncs(cuda):
+    """The default call enqueues and returns like the reference operator: no
+    host synchronisation (torch's sync debug mode turns any into an error);
+    a bad id is reported by check_status (or a later call) instead."""
+    q = torch.randn(2, 64, 64, device=cuda).to(torch.bfloat16)
+    kp = torch.randn(2, 128, 64, device=cuda).to(torch.bfloat16)
+    ks = torch.randn(2, 5, 64, device=cuda).to(torch.bfloat16)
+    heads = torch.tensor([0], device=cuda, dtype=torch.int32)
+    good = torch.tensor([[[0, 1]]], device=cuda, dtype=torch.int32)
+    bad = torch.tensor([[[0, 7]]], device=cuda, dtype=torch.int32)
+    two = torch.tensor([2], device=cuda, dtype=torch.int32)
+    vggt_sparse.check_status()  # nothing pending from earlier tests
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        for _ in range(20):
+            vggt_sparse.block_attention(q, kp, kp, ks, ks, good, two, heads)
+        vggt_sparse.block_attention(q, kp, kp, ks, ks, bad, two, heads)
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
+    with pytest.raises(ValueError, match="block id"):
+        vggt_sparse.check_status()
+    # reported once; later good calls are clean
+    vggt_sparse.block_attention(q, kp, kp, ks, ks, good, two, heads)
+    vggt_sparse.check_status()
+    # a later call raises for an earlier bad one once its status copy has landed
+    vggt_sparse.block_attention(q, kp, kp, ks, ks, bad, two, heads)
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError, match="earlier call"):
+        vggt_sparse.block_attention(q, kp, kp, ks, ks, good, two, heads)
+    vggt_sparse.check_status()
 
 
 def test_torch_ops_registration(cuda):
@@ -312,6 +362,17 @@ def test_cfg2_scale_properties(cuda):
     assert float(kept.max()) <= 1.0
     mass = (p * kept).sum(-1)
     assert float(mass.min()) >= 0.9 - 1e-5
+    # every row's ids bit-exact against the oracle's selection on the kernel's
+    # fp32 scores, and those scores against the oracle's pooled scores
+    scores = res.scores.cpu().numpy()
+    exp_idx, exp_cnt = oracle.select_mass(scores, 0.9)
+    np.testing.assert_array_equal(cnt.cpu().numpy(), exp_cnt)
+    np.testing.assert_array_equal(idx.cpu().numpy(), exp_idx[..., :idx.shape[-1]])
+    sel = np.asarray(layer.sparse_heads)
+    pq, _ = oracle.block_mean(x.q[sel].float().cpu().numpy(), 64)
+    pk, _ = oracle.block_mean(x.kp[sel].float().cpu().numpy(), 64)
+    np.testing.assert_allclose(scores, oracle.pooled_scores(pq, pk, 64 ** -0.5), rtol=1e-4,
+                               atol=1e-5)
     # sampled query blocks against the oracle
     qbs = [0, 1, 300, x.shape.n_qblocks - 1]
     rows = np.concatenate([np.arange(b * 64, min((b + 1) * 64, x.shape.n_tokens)) for b in qbs])
@@ -326,3 +387,72 @@ def test_cfg2_scale_properties(cuda):
     dense_exp = oracle.dense_attention(x.q.float().cpu().numpy()[:1], x.k.float().cpu().numpy()[:1],
                                        x.v.float().cpu().numpy()[:1], rows=rows[:128])
     check_out(torch.tensor(got[:1, rows[:128]]), dense_exp)
+
+
+def _sampled_rows_against_oracle(x, out, idx, cnt, slot_heads, dense_heads, qbs):
+    """Query blocks ``qbs`` of the given sparse (slot, head) pairs and dense
+    heads against the fp64 oracle, one head at a time (full-size layers do not
+    fit the oracle whole)."""
+    rows = np.concatenate([np.arange(b * 64, min((b + 1) * 64, x.shape.n_tokens)) for b in qbs])
+    ks, vs = x.ks.float().cpu().numpy(), x.vs.float().cpu().numpy()
+    for slot, head in slot_heads:
+        q1 = x.q[head:head + 1].float().cpu().numpy()
+        kp1 = x.kp[head:head + 1].float().cpu().numpy()
+        vp1 = x.vp[head:head + 1].float().cpu().numpy()
+        exp, _ = oracle.block_sparse_attention(
+            q1, kp1, vp1, ks[head:head + 1], vs[head:head + 1],
+            idx[slot:slot + 1].cpu().numpy(), cnt[slot:slot + 1].cpu().numpy(), [0], qblocks=qbs)
+        check_out(out[head, rows], exp[0, rows])
+    for head in dense_heads:
+        k1 = torch.cat((x.ks[head], x.kp[head])).float().cpu().numpy()[None]
+        v1 = torch.cat((x.vs[head], x.vp[head])).float().cpu().numpy()[None]
+        exp = oracle.dense_attention(x.q[head:head + 1].float().cpu().numpy(), k1, v1, rows=rows)
+        check_out(out[head, rows], exp[0])
+
+
+def test_cfg4_full_masks_and_sampled_attention(cuda):
+    """Config 4 (100 frames, 137,400 tokens, top-k 15 % = 315 of 2,140 key
+    blocks, all heads sparse) at full size: every row's ids bit-exact against
+    the oracle's top-k on the kernel's fp32 scores, and the first, a middle and
+    the last query block of three heads against the fp64 oracle."""
+    x = clustered_layer(100, centres=256, seed=0, device=cuda)
+    layer = vggt_sparse.SparseGlobalLayer(16, mode="topk", retention=0.15)
+    layer.topk = vggt_sparse.topk_budget(0.15, x.shape.n_tokens, x.shape.n_special,
+                                         x.shape.n_blocks, 64)
+    assert layer.topk == 315
+    out = layer(x.q, x.kp, x.vp, x.ks, x.vs)
+    idx, cnt = layer.last_masks
+    res = vggt_sparse.block_mask_estimate(x.q, x.kp, head_ids=layer.sparse_heads, mode="topk",
+                                          topk=315, export_scores=True)
+    assert torch.equal(res.indices, idx) and torch.equal(res.counts, cnt)
+    assert bool((cnt == 315).all())
+    exp = oracle.select_topk(res.scores.cpu().numpy(), 315)
+    np.testing.assert_array_equal(idx.cpu().numpy(), exp)
+    qbc = x.shape.n_qblocks
+    _sampled_rows_against_oracle(x, out, idx, cnt, [(0, 0), (7, 7), (15, 15)], [],
+                                 [0, qbc // 2, qbc - 1])
+
+
+def test_cfg5_sampled_masks_and_attention(cuda):
+    """Config 5 (256 frames, 351,744 tokens, mass 0.85 over 5,476 key blocks,
+    heads 0-3 dense) at full size on one GPU: sampled rows' ids bit-exact
+    against the oracle's mass rule on the kernel's fp32 scores, and the first,
+    a middle and the last query block of a sparse and a dense head against the
+    fp64 oracle."""
+    x = clustered_layer(256, centres=512, seed=0, device=cuda)
+    layer = vggt_sparse.SparseGlobalLayer(16, mode="mass", tau=0.85, dense_heads=(0, 1, 2, 3))
+    out = layer(x.q, x.kp, x.vp, x.ks, x.vs)
+    idx, cnt = layer.last_masks
+    qbc = x.shape.n_qblocks
+    qbs = [0, qbc // 2, qbc - 1]
+    res = vggt_sparse.block_mask_estimate(x.q, x.kp, head_ids=layer.sparse_heads, mode="mass",
+                                          tau=0.85, export_scores=True)
+    assert torch.equal(res.indices, idx) and torch.equal(res.counts, cnt)
+    pick = [0, 1, 2, 1000, qbc // 2, qbc - 2, qbc - 1]
+    scores = res.scores[:, pick].cpu().numpy()
+    exp_idx, exp_cnt = oracle.select_mass(scores, 0.85)
+    np.testing.assert_array_equal(cnt[:, pick].cpu().numpy(), exp_cnt)
+    np.testing.assert_array_equal(idx[:, pick].cpu().numpy(), exp_idx[..., :idx.shape[-1]])
+    del res
+    # slot 0 is head 4 (the first sparse head), slot 11 head 15
+    _sampled_rows_against_oracle(x, out, idx, cnt, [(0, 4), (11, 15)], [0], qbs)

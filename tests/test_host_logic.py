@@ -1,5 +1,6 @@
 """Host-side logic: layout, head profiles, budgets, configs, synthetic data."""
 import json
+import os
 import math
 
 import numpy as np
@@ -85,3 +86,24 @@ def test_layer_flop_count_formula():
     flops = layer.kept_flops(100, 90, 10, 8)
     expect = 4 * 8 * (64 * (64 + 10) + 36 * (26 + 10)) + 4 * 8 * 100 * 100
     assert flops == expect
+
+
+def test_head_profile_parser_on_the_reference_profile():
+    """The reference's shipped VGGT profile (an unmodified copy,
+    tests/golden/head_profile_eth3d.json): per layer, the parser assigns every
+    head the mode the reference's own wrapper assigns
+    (tests/golden/make_profile_golden.py), and leaves the profile unchanged."""
+    import copy
+    from conftest import GOLDEN
+    path = os.path.join(GOLDEN, "head_profile_eth3d.json")
+    g = np.load(os.path.join(GOLDEN, "head_profile.npz"))
+    with open(path) as f:
+        profile = json.load(f)
+    before = copy.deepcopy(profile)
+    assert len(g["layers"]) == 24
+    for layer, want in zip(g["layers"], g["modes"]):
+        assert prof.head_modes_from_profile(profile, int(layer), 16) == list(want)
+        assert prof.head_modes_from_profile(path, int(layer), 16) == list(want)
+        dense = prof.dense_heads_from_profile(profile, int(layer), 16)
+        assert dense == [h for h, m in enumerate(want) if m == "full"]
+    assert profile == before

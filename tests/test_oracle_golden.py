@@ -174,3 +174,39 @@ def test_reference_layer_masks_are_topk_of_its_routing():
     for head in range(g["masks"].shape[0]):
         ours = oracle.select_topk(g["routing"][head], g["masks"].shape[-1])
         np.testing.assert_array_equal(ours, g["masks"][head])
+
+
+def _boundary_mismatches(scores, counts, ref_m, tau):
+    """Rows whose kept count differs from the reference's fp32 rule, and the
+    largest distance from tau of the float64 cumulative mass at the boundary
+    of each such row (the rule is m = #(cumsum < tau) + 1)."""
+    x = scores.astype(np.float64)
+    p = np.exp(x - x.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    cum = np.cumsum(np.sort(p, 1)[:, ::-1], 1)
+    rows, worst = [], 0.0
+    for r in range(scores.shape[0]):
+        if counts[r] != ref_m[r]:
+            lo, hi = sorted((int(counts[r]), int(ref_m[r])))
+            # every cumulative mass between the two counts sits at tau
+            gap = np.abs(cum[r, lo - 1:hi - 1] - tau).max()
+            rows.append(r)
+            worst = max(worst, gap)
+    return rows, worst
+
+
+@pytest.mark.parametrize("cfg,tau", [("cfg2", 0.9), ("cfg2", 0.85), ("cfg5", 0.85),
+                                     ("cfg5", 0.9)])
+def test_mass_rule_on_layer_sized_rows(cfg, tau):
+    """Pooled-score rows of the 32- and 256-frame layers (685 and 5,476 key
+    blocks; tests/golden/make_mass_golden.py): the oracle's quantised mass rule
+    keeps the same count as the reference's fp32 softmax + concentration
+    except on rows whose cumulative mass at the boundary lies within fp32
+    rounding of tau (a few ulps of a sum of thousands of fp32 terms)."""
+    g = load_golden("mass_rows.npz")
+    scores = g["%s_scores" % cfg]
+    ref_m = g["%s_m%d" % (cfg, round(tau * 100))]
+    _, counts = oracle.select_mass(scores, tau)
+    rows, worst = _boundary_mismatches(scores, counts, ref_m, tau)
+    assert worst < 2e-6, (rows, worst)
+    assert len(rows) <= max(1, scores.shape[0] // 20), rows
