@@ -61,6 +61,28 @@ int vggt_sparse_version(void);
 const char* vggt_sparse_last_error(void);
 
 /*
+ * Failure detection.  No counterpart in the reference, whose Triton kernels
+ * have no pipeline waits.  Every wait inside the tcgen05 attention kernels
+ * (a TMA copy landing, an MMA finishing, a softmax warp publishing P) gives
+ * up after this many nanoseconds; the launch then sets VGGT_STATUS_TIMEOUT,
+ * lets its copies and MMAs in flight finish, releases its tensor memory and
+ * returns, leaving the context usable (the output is invalid).  0 restores
+ * the default of one second.  Process-wide; applies to launches enqueued
+ * after the call.  Returns the previous setting.
+ */
+uint64_t vggt_sparse_set_wait_limit_ns(uint64_t ns);
+
+/*
+ * Self-test of the failure path above (no counterpart in the reference).
+ * While enabled (nonzero), every tcgen05 attention launch first waits on a
+ * barrier that nothing completes, so each of its CTAs runs out of its wait
+ * limit and takes the abort path: VGGT_STATUS_TIMEOUT is set, nothing is
+ * left in flight, the output is invalid and the context stays usable.  Meant
+ * for tests, with a short wait limit.  Returns the previous setting.
+ */
+int vggt_sparse_set_wait_selftest(int enable);
+
+/*
  * Block-sparse attention forward (with optional same-pass evidence).
  * Replaces saf3r/triton/adaptive_block_attention.py:63-83 (block_attention)
  * and its Triton kernel _forward (:7-60).

@@ -25,7 +25,8 @@
 //  * dense-profiled slots walk every patch block (no index reads): the dense
 //    path of the same kernel.
 //
-// Every mbarrier wait is bounded (1 s); on expiry the CTA raises an abort
+// Every mbarrier wait is bounded (Params.wait_ns, 1 s by default; the drains
+// below always allow 1 s); on expiry the CTA raises an abort
 // flag, records VGGT_STATUS_TIMEOUT, drains its in-flight copies, frees its
 // TMEM and exits.
 #include <cuda.h>
@@ -69,7 +70,8 @@ constexpr int B_PFULL = B_SFULL + 2;          // [2]
 constexpr int B_PVDONE = B_PFULL + 2;         // one phase per PV MMA
 constexpr int B_OFULL = B_PVDONE + 1;         // the last PV MMA is done
 constexpr int B_DRAIN = B_OFULL + 1;          // MMA completion before TMEM release
-constexpr int NBAR = B_DRAIN + 1;
+constexpr int B_NEVER = B_DRAIN + 1;          // nothing arrives (wait self-test)
+constexpr int NBAR = B_NEVER + 1;
 constexpr uint32_t OFF_META = OFF_BAR + NBAR * 8;       // int[NSTAGE]
 constexpr uint32_t OFF_MISC = OFF_META + NSTAGE * 4;    // tmem base, abort, tiles, scratch
 // evidence partials: float[4 ring][2 query blocks][2 warps] + int counters[4][2]
@@ -99,6 +101,10 @@ struct Params {
   int64_t* part_rows;
   int counts_per_qblock;
   float scale_log2;
+  uint64_t wait_ns;  // limit of every pipeline wait (the drains keep WAIT_LIMIT_NS)
+  // failure-detection self-test: the MMA issuer first waits on B_NEVER, which
+  // runs out after wait_ns and aborts the CTA through the normal path
+  int wait_selftest;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -305,6 +311,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc::mbar_init(bar(B_PVDONE), 1);
     tc::mbar_init(bar(B_OFULL), 1);
     tc::mbar_init(bar(B_DRAIN), 1);
+    tc::mbar_init(bar(B_NEVER), 1);
     misc[1] = 0u;  // abort flag
     for (int i = 0; i < 8; ++i) ev_cnt[i] = 0;
     tc::mbar_fence_init();
@@ -365,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int stage = (int)(t % NSTAGE);
         if (t >= NSTAGE) {
           if (!tc::mbar_wait(bar(B_KVEMPTY + stage), (uint32_t)((t / NSTAGE - 1) & 1), abort_flag,
-                             WAIT_LIMIT_NS))
+                             p.wait_ns))
             break;
         }
         int flags, ncols, row;
@@ -411,9 +418,10 @@ __global__ void __launch_bounds__(THREADS, 2)
                         (int)head);
         ++issued;
       }
-      if (*abort_flag) {
-        // drain: wait (bounded) for every copy this thread issued
-        tc::mbar_wait_drain(bar(B_QFULL), 0, WAIT_LIMIT_NS);
+      {
+        // drain: wait (bounded) for the last NSTAGE copies, landed or not, so
+        // none is in flight when the CTA exits (after an abort the consumers
+        // stop waiting for them; their completion depends on the copy alone)
         const int64_t first = issued > NSTAGE ? issued - NSTAGE : 0;
         for (int64_t t = first; t < issued; ++t)
           tc::mbar_wait_drain(bar(B_KVFULL + (int)(t % NSTAGE)), (uint32_t)((t / NSTAGE) & 1),
@@ -426,12 +434,13 @@ __global__ void __launch_bounds__(THREADS, 2)
       const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       const uint32_t id_qk = tc::idesc_f16(fmt, 0u, BM, BN);
       const uint32_t id_pv = tc::idesc_f16(fmt, 1u, BM, ON);
-      bool ok = tc::mbar_wait(bar(B_QFULL), 0, abort_flag, WAIT_LIMIT_NS);
+      bool ok = tc::mbar_wait(bar(B_QFULL), 0, abort_flag, p.wait_ns);
+      if (p.wait_selftest) ok = ok && tc::mbar_wait(bar(B_NEVER), 0, abort_flag, p.wait_ns);
       // O (TMEM) += P_u V_u; the first PV of the CTA initialises O.
       auto issue_pv = [&](int64_t u) -> bool {
         const int bu = (int)(u & 1);
         const int su = (int)(u % NSTAGE);
-        if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, WAIT_LIMIT_NS))
+        if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, p.wait_ns))
           return false;
         tc::tc_fence_after();
         // MN group 0 = the V tile, group 1 (LBO bytes further) = the ones tile
@@ -449,7 +458,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int stage = (int)(t % NSTAGE);
         const int b = (int)(t & 1);
         if (!tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
-                           WAIT_LIMIT_NS)) {
+                           p.wait_ns)) {
           ok = false;
           break;
         }
@@ -510,9 +519,9 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int stage = (int)(t % NSTAGE);
       const int b = (int)(t & 1);
       bool got = tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
-                               WAIT_LIMIT_NS) &&
+                               p.wait_ns) &&
                  tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1), abort_flag,
-                               WAIT_LIMIT_NS);
+                               p.wait_ns);
       // keep the warp converged for the .sync.aligned TMEM instructions
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
@@ -551,7 +560,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           // O must hold every PV issued so far (through tile t-1) before it is
           // rescaled; PV_t cannot start before P_t is published below.
           const bool done = tc::mbar_wait(bar(B_PVDONE), (uint32_t)((t - 1) & 1), abort_flag,
-                                          WAIT_LIMIT_NS);
+                                          p.wait_ns);
           if (!__all_sync(0xffffffffu, done)) {
             ok = false;
             break;
@@ -648,7 +657,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 
     // ---- epilogue: O / l -> out ----
     if (ok && n_tiles > 0)
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(bar(B_OFULL), 0, abort_flag, WAIT_LIMIT_NS));
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(bar(B_OFULL), 0, abort_flag, p.wait_ns));
     tc::tc_fence_after();
     const int64_t qrow = my_qb * 64 + (row & 63);
     const bool valid_row = ok && my_qb >= 0 && qrow < p.n_tokens;
@@ -836,6 +845,17 @@ static cudaError_t launch_kernel(int64_t grid, size_t smem, cudaStream_t stream,
   return cudaGetLastError();
 }
 
+cudaError_t launch_combine_splits(const AttnArgs& a, int64_t items, int nsplit,
+                                  cudaStream_t stream) {
+  if (a.dtype == VGGT_DTYPE_BF16)
+    tcattn::combine_splits_kernel<__nv_bfloat16><<<(unsigned)items, 128, 0, stream>>>(
+        a.partial, a.part_rows, nsplit, static_cast<__nv_bfloat16*>(a.out));
+  else
+    tcattn::combine_splits_kernel<__half><<<(unsigned)items, 128, 0, stream>>>(
+        a.partial, a.part_rows, nsplit, static_cast<__half*>(a.out));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   using namespace tcattn;
   if (a.n_slots == 0 || a.qb_count == 0) return cudaSuccess;
@@ -873,6 +893,8 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
   p.partial = a.partial;
   p.part_rows = a.part_rows;
   p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.wait_ns = a.wait_ns > 0 ? a.wait_ns : WAIT_LIMIT_NS;
+  p.wait_selftest = a.wait_selftest;
   const bool evid = a.evidence != nullptr;
   const size_t smem = 1024 + OFF_BITMAP + 2 * (size_t)((a.nb + 31) / 32) * 4 +
                       (evid ? 2 * (size_t)((a.nb + 7) & ~7LL) * 2 : 0);
@@ -887,15 +909,8 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream) {
     e = evid ? launch_kernel<__half, true>(grid, smem, stream, mkp, mvp, mks, mvs, p)
              : launch_kernel<__half, false>(grid, smem, stream, mkp, mvp, mks, mvs, p);
   if (e != cudaSuccess) return e;
-  if (p.nsplit > 1) {
-    if (a.dtype == VGGT_DTYPE_BF16)
-      combine_splits_kernel<__nv_bfloat16><<<(unsigned)items, 128, 0, stream>>>(
-          p.partial, p.part_rows, p.nsplit, static_cast<__nv_bfloat16*>(a.out));
-    else
-      combine_splits_kernel<__half><<<(unsigned)items, 128, 0, stream>>>(
-          p.partial, p.part_rows, p.nsplit, static_cast<__half*>(a.out));
-  }
-  return cudaGetLastError();
+  if (p.nsplit > 1) return launch_combine_splits(a, items, p.nsplit, stream);
+  return cudaSuccess;
 }
 
 int64_t attn_tc05_split(int64_t items, int sms) {

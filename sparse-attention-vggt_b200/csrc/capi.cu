@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -19,6 +20,12 @@
 namespace {
 
 thread_local char g_err[512] = "";
+
+// limit of every pipeline wait in the tcgen05 attention kernels (0: the
+// kernels' default of one second); see vggt_sparse_set_wait_limit_ns
+std::atomic<uint64_t> g_wait_ns{0};
+// see vggt_sparse_set_wait_selftest
+std::atomic<int> g_wait_selftest{0};
 
 int fail(const char* fmt, ...) {
   va_list ap;
@@ -63,6 +70,12 @@ int64_t attention_split(int64_t items) {
 extern "C" {
 
 int vggt_sparse_version(void) { return (1 << 16) | 0; }
+
+uint64_t vggt_sparse_set_wait_limit_ns(uint64_t ns) { return g_wait_ns.exchange(ns); }
+
+int vggt_sparse_set_wait_selftest(int enable) {
+  return g_wait_selftest.exchange(enable ? 1 : 0);
+}
 
 const char* vggt_sparse_last_error(void) { return g_err; }
 
@@ -146,6 +159,8 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
   a.nsplit = 1;
   a.partial = nullptr;
   a.part_rows = nullptr;
+  a.wait_ns = g_wait_ns.load();
+  a.wait_selftest = g_wait_selftest.load();
   if (a.qb_count > 0x7fffffffLL) return fail("too many query blocks");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc_ok = vggt::attn_tc05_supported(a);

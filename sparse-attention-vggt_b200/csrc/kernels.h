@@ -50,6 +50,11 @@ struct AttnArgs {
   int64_t n_slots, max_blocks, qb_count, nb;
   int dim, block_q, block_k, dtype, counts_per_qblock;
   float scale;
+  // limit of every pipeline wait of the tcgen05 kernels (0: one second)
+  uint64_t wait_ns;
+  // nonzero: the tcgen05 kernel's MMA issuer first waits on a barrier that
+  // nothing completes, so every CTA takes the timeout path (self-test)
+  int wait_selftest;
 };
 
 // pairing.cu: query-block pairing for the 128-row tcgen05 tiles
@@ -115,5 +120,8 @@ cudaError_t launch_attn_tc05(const AttnArgs& a, cudaStream_t stream);
 // nsplit <= 1)
 int64_t attn_tc05_split(int64_t items, int sms);
 size_t attn_tc05_split_bytes(int64_t items, int64_t nsplit);
+// merge launch of a key-range split (one CTA per work item)
+cudaError_t launch_combine_splits(const AttnArgs& a, int64_t items, int nsplit,
+                                  cudaStream_t stream);
 
 }  // namespace vggt

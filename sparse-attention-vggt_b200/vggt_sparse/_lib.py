@@ -21,6 +21,8 @@ _I = ctypes.c_int
 SIGNATURES = {
     "vggt_sparse_version": (_I, []),
     "vggt_sparse_last_error": (ctypes.c_char_p, []),
+    "vggt_sparse_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
+    "vggt_sparse_set_wait_selftest": (_I, [_I]),
     "vggt_block_attention": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P, _I,
                                   _P, _P, _I64, _I64, _I, _I, ctypes.c_float, _P, _P, _P, _I, _P]),
     "vggt_block_attention_ex": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P,
@@ -72,6 +74,20 @@ def load(path=None):
 
 def last_error():
     return load().vggt_sparse_last_error().decode()
+
+
+def set_wait_limit_ns(ns):
+    """Limit (ns) of every pipeline wait in the tcgen05 attention kernels,
+    process-wide, for launches enqueued afterwards; 0 restores the default
+    (one second).  Returns the previous setting."""
+    return int(load().vggt_sparse_set_wait_limit_ns(int(ns)))
+
+
+def set_wait_selftest(enable):
+    """While enabled, every tcgen05 attention launch waits on a barrier that
+    nothing completes and takes the timeout path (tests of failure
+    detection).  Returns the previous setting."""
+    return int(load().vggt_sparse_set_wait_selftest(1 if enable else 0))
 
 
 def check(rc):

@@ -30,7 +30,16 @@ def test_header_declares_the_documented_entry_points():
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
         "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
         "vggt_block_select", "vggt_frame_qk_topk", "vggt_history_update", "vggt_sparse_last_error",
-        "vggt_sparse_version", "vggt_token_sparse_attention"])
+        "vggt_sparse_set_wait_limit_ns", "vggt_sparse_set_wait_selftest", "vggt_sparse_version", "vggt_token_sparse_attention"])
+
+
+def test_wait_limit_setter_round_trips(lib):
+    from vggt_sparse import _lib
+    assert _lib.set_wait_limit_ns(12345) == 0
+    assert _lib.set_wait_limit_ns(0) == 12345
+    assert _lib.set_wait_limit_ns(0) == 0
+    assert _lib.set_wait_selftest(True) == 0
+    assert _lib.set_wait_selftest(False) == 1
 
 
 @pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++17")])
