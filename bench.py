@@ -9,9 +9,10 @@ block-mask estimator on the sparse heads + one block-sparse attention launch
 (sparse heads through their masks, dense-profiled heads through the dense path
 of the same kernel).  Default workload: config 2 (32 frames, 43,968 tokens,
 16 heads x 64, mass 0.9, heads 0-3 dense).  With N > 1 ranks (torchrun, one
-process per GPU, NCCL) the layer's query blocks (or heads) are split across
-ranks: total work is fixed ("strong"), no collective is needed inside the
-layer because every rank holds the full K/V of the layer.
+process per GPU, NCCL) the layer is split across ranks with total work fixed
+("strong"); by default (--shard kv-allgather) each rank starts from its own
+query blocks' rows and its own frames' K/V, and every step all-gathers K/V
+over NCCL (NVLink) before and while the rank computes its query blocks.
 
 Prints ONE JSON line on rank 0.  ``value`` is ms per layer (max over ranks).
 """
@@ -42,7 +43,12 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", default="cfg2")
-    p.add_argument("--shard", choices=("qblocks", "heads", "kv-allgather"), default="qblocks")
+    p.add_argument("--shard", choices=("kv-allgather", "qblocks", "heads"), default="kv-allgather",
+                   help="with N > 1 ranks: kv-allgather (default) = each rank holds its query "
+                        "blocks' rows and its frames' K/V and all-gathers K/V over NCCL in "
+                        "every step; qblocks = query-block shards with the layer's K/V "
+                        "replicated on every rank (no collective); heads = each rank holds "
+                        "only a cost-balanced set of heads (no collective)")
     p.add_argument("--kernel", default="auto")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -853,68 +859,69 @@ def main():
                         dtype=torch.bfloat16)
     q, kp, vp, ks, vs, dense, rows = shard_inputs(x, cfg, rank, world, args.shard, device)
     heads = q.shape[0]
-    layer = vggt_sparse.SparseGlobalLayer(heads, mode=cfg.mode, retention=cfg.retention,
-                                          tau=cfg.tau, dense_heads=dense, block=cfg.block,
-                                          kernel=args.kernel)
-    if cfg.mode == "topk":
-        # the budget follows the FULL layer size, as the reference computes it
-        layer.topk = vggt_sparse.topk_budget(cfg.retention, x.shape.n_tokens, x.shape.n_special,
-                                             x.shape.n_blocks, cfg.block)
-    out = torch.empty_like(q)
-    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
-    # estimator (pool Q, pool K, score + select), then, when the tcgen05 kernel
-    # runs with its workspace, query-block pairing (bitmaps, window costs,
-    # greedy, schedule), attention, and the merge launch of a key-range split
-    # (grids under 4 waves of 296 CTAs, or VGGT_ATTN_SPLIT > 1)
-    launches_per_step = (3 if layer.sparse_heads else 0) + 1
-    n_slots = len(layer.sparse_heads) + len(layer.dense_heads)
-    if layer.sparse_heads and layer.pair_qblocks and args.kernel != "mma_sync" and \
-            ops.attention_workspace_size(q.shape[1], kp.shape[1], n_slots) > 0:
-        launches_per_step += 4
-        items = n_slots * ((-(-q.shape[1] // cfg.block) + 1) // 2)
-        forced = os.environ.get("VGGT_ATTN_SPLIT", "")
-        wave = 2 * torch.cuda.get_device_properties(device).multi_processor_count
-        split = int(forced) if forced in ("1", "2", "3", "4") else (2 if items < 4 * wave else 1)
-        if split > 1:
-            launches_per_step += 1
-
-    gather = None
-    if args.shard == "kv-allgather" and world > 1:
-        # each rank holds the K/V of its own frames; one NCCL all-gather per
-        # tensor (inside every timed step) rebuilds the layer's full K/V
+    layer_kwargs = dict(mode=cfg.mode, retention=cfg.retention, tau=cfg.tau, block=cfg.block,
+                        kernel=args.kernel)
+    n_patch_full, n_special_full = x.shape.n_patch, x.shape.n_special
+    frame_sharded = args.shard == "kv-allgather" and world > 1
+    if frame_sharded:
+        # sequence parallel: this rank holds the query rows of its query
+        # blocks and the K/V of its frames; every step all-gathers K/V over
+        # NCCL head group by head group, overlapped with the groups' compute
         from vggt_sparse import distributed as vd
+        runner = vd.FrameShardedLayer(heads, world, rank, cfg.frames, dense_heads=dense,
+                                      **layer_kwargs)
         f0, f1 = vd.frame_range(cfg.frames, world, rank)
         ppf, spf = x.shape.patch_h * x.shape.patch_w, x.shape.special_per_frame
-        local = [x.kp[:, f0 * ppf:f1 * ppf].contiguous(), x.vp[:, f0 * ppf:f1 * ppf].contiguous(),
-                 x.ks[:, f0 * spf:f1 * spf].contiguous(), x.vs[:, f0 * spf:f1 * spf].contiguous()]
+        kp, vp = (t[:, f0 * ppf:f1 * ppf].contiguous() for t in (x.kp, x.vp))
+        ks, vs = (t[:, f0 * spf:f1 * spf].contiguous() for t in (x.ks, x.vs))
+        layers = runner.layers
+    else:
+        runner = vggt_sparse.SparseGlobalLayer(heads, dense_heads=dense, **layer_kwargs)
+        if cfg.mode == "topk":
+            # the budget follows the FULL layer size, as the reference computes it
+            runner.topk = vggt_sparse.topk_budget(cfg.retention, x.shape.n_tokens,
+                                                  x.shape.n_special, x.shape.n_blocks, cfg.block)
+        layers = [runner]
+    out = torch.empty_like(q)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
 
-        def gather():
-            return [vd.allgather_frames(t, world) for t in local]
+    def launches(layer):
+        """Our kernels per call of one layer: estimator (pool Q, pool K, score +
+        select), then, when the tcgen05 kernel runs with its workspace,
+        query-block pairing (bitmaps, window costs, greedy, schedule),
+        attention, and the merge launch of a key-range split (grids under 4
+        waves of 2 CTAs per SM, or VGGT_ATTN_SPLIT > 1)."""
+        if not layer.sparse_heads and not layer.dense_heads:
+            return 0
+        n = (3 if layer.sparse_heads else 0) + 1
+        n_slots = len(layer.sparse_heads) + len(layer.dense_heads)
+        if layer.sparse_heads and layer.pair_qblocks and args.kernel != "mma_sync" and \
+                ops.attention_workspace_size(q.shape[1], n_patch_full, n_slots) > 0:
+            n += 4
+            items = n_slots * ((-(-q.shape[1] // cfg.block) + 1) // 2)
+            forced = os.environ.get("VGGT_ATTN_SPLIT", "")
+            wave = 2 * torch.cuda.get_device_properties(device).multi_processor_count
+            split = int(forced) if forced in ("1", "2", "3", "4") else (
+                2 if items < 4 * wave else 1)
+            n += 1 if split > 1 else 0
+        return n
+    launches_per_step = sum(launches(l) for l in layers)
 
     def step(events=None):
         if events is not None:
             events[0].record()
-        if gather is None:
-            layer(q, kp, vp, ks, vs, out=out, events=None if events is None else events[1:])
+        if frame_sharded:
+            runner(q, kp, vp, ks, vs, out=out)
+            if events is not None:
+                events[3].record()
             return
-        # K first (the estimator needs it); V and the specials travel on NCCL's
-        # stream while the estimator runs, and attention waits for them
-        kp_full = vd.allgather_frames(local[0], world)
-        pending = [vd.allgather_frames_async(t, world) for t in local[1:]]
-        if events is not None:
-            events[1].record()
-        layer.estimate(q, kp_full, x.ks.shape[1])
-        if events is not None:
-            events[2].record()
-        vp_full, ks_full, vs_full = (p_.result() for p_ in pending)
-        layer.attend(q, kp_full, vp_full, ks_full, vs_full, out=out)
-        if events is not None:
-            events[3].record()
+        runner(q, kp, vp, ks, vs, out=out, events=None if events is None else events[1:])
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    flops_local = layer.kept_flops(q.shape[1], kp.shape[1], ks.shape[1], q.shape[2])
+    flops_local = sum(l.kept_flops(q.shape[1], n_patch_full, n_special_full, q.shape[2])
+                      for l in layers)
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     sampler = ClockSampler(device.index) if rank == 0 else None
@@ -935,14 +942,36 @@ def main():
     barrier(world)
     clocks = sampler.stop() if sampler else None
     step_ms = [e[0].elapsed_time(e[3]) for e in ev]
-    gather_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    est_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    att_ms = [e[2].elapsed_time(e[3]) for e in ev]
     ms_local = sum(step_ms) / len(step_ms)
     ms = reduce_max(ms_local, world)
-    att_local = sum(att_ms) / len(att_ms)
-    est_local = sum(est_ms) / len(est_ms)
+    if frame_sharded:
+        # estimator and attention of the head groups interleave with the
+        # transfers; the split is not separable by events
+        att_local = est_local = None
+    else:
+        est_ms = [e[1].elapsed_time(e[2]) for e in ev]
+        att_ms = [e[2].elapsed_time(e[3]) for e in ev]
+        att_local = sum(att_ms) / len(att_ms)
+        est_local = sum(est_ms) / len(est_ms)
     flops_total = reduce_sum(flops_local, world)
+    gather_alone = None
+    if frame_sharded:
+        # the K/V all-gather by itself (all head groups, nothing overlapped)
+        full = runner._buffers(kp, ks)
+        pairs = tuple(zip((kp, vp, ks, vs), full))
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(4):
+            barrier(world)
+            if i == 1:
+                g0.record()
+            for w in [vd.gather_heads_async(pairs, g, world) for g in runner.groups]:
+                w.wait()
+        g1.record()
+        torch.cuda.synchronize()
+        gms = reduce_max(g0.elapsed_time(g1) / 3, world)
+        gbytes = runner.gathered_bytes(kp, ks)
+        gather_alone = {"ms": gms, "bytes_received_per_rank": gbytes,
+                        "gbs_per_rank": gbytes / (gms * 1e-3) / 1e9}
 
     # end-to-end through the public API with pinned host buffers: every step
     # uploads its five inputs and downloads its output.  `value` is the
@@ -961,7 +990,7 @@ def main():
         def serial_step():
             for d_, h_ in zip(dev_in, host):
                 d_.copy_(h_, non_blocking=True)
-            o = layer(*dev_in)
+            o = runner(*dev_in)
             host_out[0].copy_(o, non_blocking=True)
 
         for _ in range(max(1, args.warmup // 2)):
@@ -977,7 +1006,7 @@ def main():
         barrier(world)
         serial_ms = reduce_max(s0.elapsed_time(s1) / e2e_steps, world)
 
-        pipe = vggt_sparse.HostPipeline(layer)
+        pipe = vggt_sparse.HostPipeline(runner)
         for i in range(max(2, args.warmup // 2)):
             pipe(*host, out=host_out[i % 2])
         pipe.synchronize()
@@ -1012,12 +1041,15 @@ def main():
             dist.destroy_process_group()
         return
     peaks = load_peaks()
-    att_tflops = flops_local / (att_local * 1e-3) / 1e12
-    n_sparse = len(layer.sparse_heads)
-    qbc = math.ceil(q.shape[1] / cfg.block)
-    idx, cnt = layer.last_masks
-    est_bytes = (n_sparse * (q.shape[1] + kp.shape[1]) * q.shape[2] * 2 +
-                 idx.numel() * 4 + cnt.numel() * 4)
+    # the attention launch alone (single layer); the whole step when the
+    # frame-sharded layer interleaves transfers, estimator and attention
+    att_tflops = flops_local / ((att_local if att_local is not None else ms_local) * 1e-3) / 1e12
+    est_bytes = 0
+    for l in layers:
+        if l.sparse_heads and l.last_masks is not None:
+            idx, cnt = l.last_masks
+            est_bytes += (len(l.sparse_heads) * (q.shape[1] + n_patch_full) * q.shape[2] * 2 +
+                          idx.numel() * 4 + cnt.numel() * 4)
     line = {
         "metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
@@ -1034,10 +1066,11 @@ def main():
         "kept_block_gflop_per_layer": flops_total / 1e9,
         "frames_per_s": cfg.frames / (ms * 1e-3),
         "estimator_ms": est_local, "attention_ms": att_local,
-        "allgather_ms": (sum(gather_ms) / len(gather_ms)) if gather is not None else None,
-        "allgather": ("K all-gathered before the estimator (allgather_ms); V and the specials "
-                      "travel while the estimator runs, any remaining wait is in attention_ms")
-                     if gather is not None else None,
+        "allgather": ({"what": "K/V (patch and special) of the other ranks' frames, one NCCL "
+                                "all-gather per head and tensor coalesced per head group, dense "
+                                "heads' group first; the sparse heads' transfer overlaps the "
+                                "dense heads' attention",
+                       "alone": gather_alone} if frame_sharded else None),
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": att_tflops / peaks["bf16_tflops"],
@@ -1048,11 +1081,11 @@ def main():
                                        "measured in this run" % args.config,
                      "flops_per_launch": flops_local,
                      "peak_source": peaks["source"] + " bf16 burst"},
-        "estimator_roofline": {"bound": "hbm", "achieved": est_bytes / (est_local * 1e-3) / 1e9,
-                               "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                               "frac": est_bytes / (est_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                               "bytes_per_step": est_bytes,
-                               "peak_source": peaks["source"]},
+        "estimator_roofline": ({"bound": "hbm", "achieved": est_bytes / (est_local * 1e-3) / 1e9,
+                                "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                "frac": est_bytes / (est_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                "bytes_per_step": est_bytes,
+                                "peak_source": peaks["source"]} if est_local else None),
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,

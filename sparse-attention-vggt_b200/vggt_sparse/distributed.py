@@ -11,6 +11,10 @@ scripts/run_scannet50_all_gpus.sh:9); the layouts here are new:
   only its own tokens' K/V) one all-gather of K and V precedes the layer.
 * head sharding: rank r owns a set of heads (all tokens), balanced by cost so
   dense-profiled heads are spread out.  No collective inside attention.
+* frame sharding (sequence parallel, ``FrameShardedLayer``): rank r owns the
+  query blocks of its rows and the K/V of its frames; every call all-gathers
+  K/V head by head straight into the layout the kernels read, pipelined by
+  head groups so later groups' transfers overlap earlier groups' compute.
 """
 import math
 
@@ -132,3 +136,112 @@ class HeadShardedLayer:
             self.layer.topk = topk_budget(self.layer.retention, q.shape[1], ks.shape[1], nb,
                                           self.layer.block)
         return self.layer(*sel, out=out), self.heads
+
+
+def gather_heads_async(pairs, heads, world, group=None):
+    """All-gather, for each head h in ``heads`` and each (local, full) pair,
+    the frame shard local[h] ([n_local, d]) into full[h] ([world * n_local,
+    d]): ranks' shards land rank-major, which for frame-major rows is the
+    layer's row order, so full[h] needs no reordering.  With NCCL the calls
+    of one invocation are coalesced into one launch on NCCL's stream; returns
+    a handle whose ``wait()`` makes the current stream wait for them."""
+    import torch.distributed as dist
+    backend = dist.get_backend(group)
+    calls = [(full[h], local[h]) for h in heads for local, full in pairs]
+    if backend == "nccl":
+        dev = calls[0][1].device if calls else None
+        with dist._coalescing_manager(group=group, device=dev, async_ops=True) as cm:
+            for dst, src in calls:
+                dist.all_gather_into_tensor(dst, src, group=group)
+        return cm
+    works = [dist.all_gather_into_tensor(dst, src, group=group, async_op=True)
+             for dst, src in calls]
+
+    class _Works:
+        def wait(self):
+            for w in works:
+                w.wait()
+    return _Works()
+
+
+class FrameShardedLayer:
+    """The layer with its K/V sharded by frames and its query blocks split
+    across ranks (sequence parallel: what a QKV projection applied to each
+    rank's own frames leaves on each GPU).
+
+    ``__call__(q_local, kp_local, vp_local, ks_local, vs_local, out=None)``
+    takes this rank's query rows ``rows(n_tokens)`` of q and the patch /
+    special K/V of its frames ``frame_range`` (every rank the same number of
+    frames), and returns this rank's output rows.  K and V are all-gathered over NCCL into
+    head-major buffers, one head group at a time in ``groups`` order; group
+    g+1's transfer runs on NCCL's stream while group g's estimator and
+    attention run.  The default order puts the dense-profiled heads first:
+    they need no estimator, so the sparse heads' transfer hides behind them.
+    """
+
+    def __init__(self, heads, world, rank, frames, *, dense_heads=(), groups=None, group=None,
+                 **layer_kwargs):
+        if frames % world:
+            raise ValueError("frames (%d) must divide evenly over %d ranks" % (frames, world))
+        self.world, self.rank, self.frames, self.group = world, rank, frames, group
+        dense = sorted(set(int(h) for h in dense_heads))
+        if groups is None:
+            rest = [h for h in range(heads) if h not in set(dense)]
+            groups = [g for g in (dense, rest) if g]
+        flat = sorted(h for g in groups for h in g)
+        if flat != list(range(heads)):
+            raise ValueError("groups must cover every head exactly once")
+        self.groups = [list(g) for g in groups]
+        self.heads = heads
+        self.layers = [SparseGlobalLayer(heads, dense_heads=dense, head_subset=g, **layer_kwargs)
+                       for g in self.groups]
+        self._full = {}
+
+    @property
+    def block(self):
+        return self.layers[0].block
+
+    def rows(self, n_tokens):
+        b0, b1 = qblock_range(math.ceil(n_tokens / self.block), self.world, self.rank)
+        return b0 * self.block, min(n_tokens, b1 * self.block)
+
+    def gathered_bytes(self, kp_local, ks_local):
+        """Bytes this rank receives per call (the other ranks' shards)."""
+        per = (kp_local.numel() + ks_local.numel()) * kp_local.element_size() * 2
+        return per * (self.world - 1)
+
+    def _buffers(self, kp_local, ks_local):
+        key = (kp_local.device, kp_local.shape, ks_local.shape, kp_local.dtype)
+        buf = self._full.get(key)
+        if buf is None:
+            h, npl, d = kp_local.shape
+            nsl = ks_local.shape[1]
+            mk = lambda n: torch.empty((h, self.world * n, d), device=kp_local.device,
+                                       dtype=kp_local.dtype)
+            buf = (mk(npl), mk(npl), mk(nsl), mk(nsl))
+            self._full[key] = buf
+        return buf
+
+    def __call__(self, q_local, kp_local, vp_local, ks_local, vs_local, out=None):
+        # every rank holds the same number of frames
+        n_tokens = self.world * (kp_local.shape[1] + ks_local.shape[1])
+        kp, vp, ks, vs = self._buffers(kp_local, ks_local)
+        pairs = ((kp_local, kp), (vp_local, vp), (ks_local, ks), (vs_local, vs))
+        for layer in self.layers:
+            if layer.mode == "topk" and layer.topk is None:
+                # the budget follows the FULL layer, as the reference computes it
+                from .layer import topk_budget
+                nb = math.ceil(kp.shape[1] / layer.block)
+                layer.topk = topk_budget(layer.retention, n_tokens, ks.shape[1], nb, layer.block)
+        # every group's transfer is enqueued up front; each group's compute
+        # waits only for its own heads
+        pending = [gather_heads_async(pairs, g, self.world, self.group) for g in self.groups]
+        if out is None:
+            out = torch.empty_like(q_local)
+        for layer, work in zip(self.layers, pending):
+            work.wait()
+            layer(q_local, kp, vp, ks, vs, out=out)
+        return out
+
+    def kept_flops(self, n_tokens, n_patch, n_special, dim):
+        return sum(l.kept_flops(n_tokens, n_patch, n_special, dim) for l in self.layers)

@@ -27,10 +27,12 @@ class SparseGlobalLayer:
     mode 'topk' keeps topk_budget(retention) blocks per query block (or an
     explicit ``topk``); mode 'mass' keeps the smallest prefix of pooled-score
     softmax mass >= tau.  ``dense_heads`` go through the dense path.
+    ``head_subset`` restricts the layer to some heads (their K/V alone need
+    to be in place when it runs).
     """
 
     def __init__(self, heads, *, mode="topk", retention=0.25, topk=None, tau=0.9,
-                 dense_heads=(), block=64, kernel="auto", evidence=False):
+                 dense_heads=(), block=64, kernel="auto", evidence=False, head_subset=None):
         if mode not in ("topk", "mass"):
             raise ValueError("mode must be 'topk' or 'mass'")
         self.heads = heads
@@ -39,6 +41,13 @@ class SparseGlobalLayer:
         self.kernel = kernel
         self.evidence = evidence
         self.sparse_heads, self.dense_heads = split_heads(heads, dense_heads)
+        if head_subset is not None:
+            # serve only these heads (the others' rows of `out` are not written)
+            keep = set(int(h) for h in head_subset)
+            if not keep <= set(range(heads)):
+                raise ValueError("head_subset must name heads in [0, %d)" % heads)
+            self.sparse_heads = [h for h in self.sparse_heads if h in keep]
+            self.dense_heads = [h for h in self.dense_heads if h in keep]
         self.workspace = EstimatorWorkspace()
         self._cache = {}
         self.last_masks = None
@@ -63,15 +72,18 @@ class SparseGlobalLayer:
             cap = mask_capacity(self.mode, k or nb, nb)
             s = len(self.sparse_heads)
             slots = self.sparse_heads + self.dense_heads
+            # a layer of dense slots only still passes one (never read) slot of
+            # indices and counts: the C ABI takes no NULL mask pointers
+            sa = max(s, 1)
             buf = dict(
                 topk=k,
-                indices=torch.empty((s, qbc, cap), device=device, dtype=torch.int32),
-                counts=torch.empty((s, qbc), device=device, dtype=torch.int32),
+                indices=torch.full((sa, qbc, cap), -1, device=device, dtype=torch.int32),
+                counts=torch.zeros((sa, qbc), device=device, dtype=torch.int32),
                 sparse_ids=torch.tensor(self.sparse_heads, device=device, dtype=torch.int32),
                 slot_ids=torch.tensor(slots, device=device, dtype=torch.int32),
                 dense_flags=torch.tensor([0] * s + [1] * len(self.dense_heads), device=device,
                                          dtype=torch.uint8),
-                evidence=torch.empty((s, qbc, cap), device=device, dtype=torch.float32),
+                evidence=torch.empty((sa, qbc, cap), device=device, dtype=torch.float32),
             )
             ws = ops.attention_workspace_size(n_tokens, n_patch, len(slots), self.block,
                                               self.block) if s else 0
@@ -109,7 +121,8 @@ class SparseGlobalLayer:
                                    buf["slot_ids"], head_dense=buf["dense_flags"],
                                    query_block=self.block, key_block=self.block, out=out,
                                    evidence=evidence, kernel=self.kernel,
-                                   pair_qblocks=self.pair_qblocks, workspace=buf["attn_ws"])
+                                   pair_qblocks=self.pair_qblocks and bool(self.sparse_heads),
+                                   workspace=buf["attn_ws"])
         self.last_masks = (buf["indices"], buf["counts"])
         self.last_evidence = evidence
         return out
@@ -129,7 +142,10 @@ class SparseGlobalLayer:
 
     def kept_flops(self, n_tokens, n_patch, n_special, dim):
         """Algorithmic FLOPs of the last call: 4*d*sum(valid rows x (kept valid
-        keys + specials)) over sparse heads + 4*d*N*N per dense head."""
+        keys + specials)) over sparse heads + 4*d*rows*(n_patch + n_special)
+        per dense head (4*d*N*N for a whole layer).  ``n_tokens`` is the
+        number of query rows of the call (a shard's rows under query-block
+        sharding)."""
         bq = bk = self.block
         qbc = math.ceil(n_tokens / bq)
         nb = math.ceil(n_patch / bk)
@@ -143,5 +159,5 @@ class SparseGlobalLayer:
             cols = torch.where(idx == nb - 1, float(last_cols), float(bk)).double() * slot
             keys = cols.sum(-1) + n_special
             total += 4.0 * dim * float((keys * rows[None]).sum())
-        total += 4.0 * dim * float(n_tokens) * float(n_tokens) * len(self.dense_heads)
+        total += 4.0 * dim * float(n_tokens) * float(n_patch + n_special) * len(self.dense_heads)
         return total

@@ -1,7 +1,10 @@
 """Running the layer on host (pinned) tensors with the transfers overlapped.
 
 ``HostPipeline(layer)`` takes each call's inputs in pinned host memory and
-writes the output to a pinned host tensor.  Uploads run on one copy stream,
+writes the output to a pinned host tensor.  ``layer`` is a SparseGlobalLayer
+(estimator and attention run as two steps) or any layer called as
+``layer(q, kp, vp, ks, vs, out=...)``, such as a FrameShardedLayer fed this
+rank's shards.  Details for a SparseGlobalLayer: uploads run on one copy stream,
 the download on another, the layer on the caller's current stream:
 
 * q and the patch keys go up first, so the estimator starts while V and the
@@ -65,10 +68,14 @@ class HostPipeline:
             dks.copy_(ks, non_blocking=True)
             dvs.copy_(vs, non_blocking=True)
             up_rest.record()
-        compute.wait_event(up_qk)
-        self.layer.estimate(dq, dkp, dks.shape[1])
-        compute.wait_event(up_rest)
-        self.layer.attend(dq, dkp, dvp, dks, dvs, out=dout)
+        if hasattr(self.layer, "estimate"):
+            compute.wait_event(up_qk)
+            self.layer.estimate(dq, dkp, dks.shape[1])
+            compute.wait_event(up_rest)
+            self.layer.attend(dq, dkp, dvp, dks, dvs, out=dout)
+        else:  # a layer that runs as one call (e.g. FrameShardedLayer)
+            compute.wait_event(up_rest)
+            self.layer(dq, dkp, dvp, dks, dvs, out=dout)
         done = torch.cuda.Event()
         done.record(compute)
         freed = torch.cuda.Event()

@@ -1,6 +1,7 @@
 """Partitioning host logic on CPU: shard ranges, head balancing, the frame
-all-gather (world 2, gloo), and that per-rank query-block shards of the oracle
-layer reassemble the full-layer result."""
+all-gather and the head-wise gathers of FrameShardedLayer (world 2, gloo), and
+that per-rank query-block shards of the oracle layer reassemble the full-layer
+result."""
 import os
 import socket
 
@@ -71,6 +72,18 @@ def _work(rank, world, result_q):
     pending = vd.allgather_frames_async(x.vp[:, f0 * per_frame_patch:f1 * per_frame_patch], world)
     vp_full = pending.result()
     gather_ok = torch.equal(kp_full, x.kp) and torch.equal(vp_full, x.vp)
+    # head-wise gathers straight into head-major buffers, two head groups in
+    # reverse order (what FrameShardedLayer enqueues)
+    spf = 5
+    locals_ = [x.kp[:, f0 * per_frame_patch:f1 * per_frame_patch].contiguous(),
+               x.vp[:, f0 * per_frame_patch:f1 * per_frame_patch].contiguous(),
+               x.ks[:, f0 * spf:f1 * spf].contiguous(), x.vs[:, f0 * spf:f1 * spf].contiguous()]
+    bufs = [torch.full_like(t, float("nan")) for t in (x.kp, x.vp, x.ks, x.vs)]
+    pairs = list(zip(locals_, bufs))
+    works = [vd.gather_heads_async(pairs, g, world) for g in ([1], [0])]
+    for w in works:
+        w.wait()
+    gather_ok = gather_ok and all(torch.equal(b, t) for b, t in zip(bufs, (x.kp, x.vp, x.ks, x.vs)))
     # query-block shard of the oracle layer
     n = x.shape.n_tokens
     b0, b1 = vd.qblock_range(-(-n // 64), world, rank)

@@ -1,5 +1,6 @@
 """Two-GPU partitioning on real devices (NCCL): query-block shards, head
-shards and the frame all-gather reproduce the single-GPU layer exactly.
+shards, the frame all-gather and the sequence-parallel (frame-sharded) layer
+reproduce the single-GPU layer exactly.
 Skipped unless at least two GPUs are visible."""
 import datetime
 import os
@@ -52,6 +53,15 @@ def _worker(rank, world, port, result_q):
         ppf = 37 * 37
         kp_full = vd.allgather_frames(x.kp[:, f0 * ppf:f1 * ppf].contiguous(), world)
         ok["allgather"] = bool(torch.equal(kp_full, x.kp))
+        # sequence-parallel layer: this rank's query rows and its own frames'
+        # K/V in, NCCL all-gathers of K/V (by head group) inside the call
+        fs = vd.FrameShardedLayer(16, world, rank, 4, **kw)
+        s0, s1 = fs.rows(x.shape.n_tokens)
+        spf = 5
+        shards = [t[:, f0 * ppf:f1 * ppf].contiguous() for t in (x.kp, x.vp)] + \
+                 [t[:, f0 * spf:f1 * spf].contiguous() for t in (x.ks, x.vs)]
+        fs_out = fs(x.q[:, s0:s1].contiguous(), *shards)
+        ok["frames"] = bool(torch.equal(fs_out, full[:, s0:s1]))
         torch.cuda.synchronize()
         result_q.put((rank, ok))
     except Exception as e:  # report instead of leaving the peer waiting
@@ -74,4 +84,5 @@ def test_two_gpu_shards_match_single_gpu_layer():
     for p in procs:
         p.join(timeout=60)
     for rank, ok in results.items():
-        assert ok == {"qblocks": True, "heads": True, "allgather": True}, (rank, ok)
+        assert ok == {"qblocks": True, "heads": True, "allgather": True, "frames": True}, \
+            (rank, ok)
