@@ -55,7 +55,7 @@ def parse_args():
     p.add_argument("--cpu-sample-blocks", type=int, default=48)
     p.add_argument("--component",
                    choices=("layer", "assembly", "triton-ref", "token-ref", "qk-topk",
-                            "aggregator"),
+                            "aggregator", "qkv"),
                    default="layer",
                    help="layer: estimator + attention (the headline); assembly: mask "
                         "assembly with history and value order + the history update; "
@@ -65,7 +65,9 @@ def parse_args():
                         "installed) the reference's Triton kernels; qk-topk: per-frame QK "
                         "top-k, this library and the reference's Triton kernel; aggregator: "
                         "config 3, the reference's VGGT aggregator end to end with its "
-                        "Triton operator and with this drop-in")
+                        "Triton operator and with this drop-in; qkv: the layer from its "
+                        "input activations with the QKV projection + pooling fused, against "
+                        "the reference's PyTorch composition")
     p.add_argument("--qk-queries", type=int, default=0,
                    help="qk-topk: query rows (default: all 43,808 tokens of the 32 frames)")
     p.add_argument("--qk-topk", default="4,16,64",
@@ -823,6 +825,109 @@ def run_aggregator_bench(args):
     print(json.dumps(line), flush=True)
 
 
+def run_qkv_bench(args):
+    """The layer from its input activations x (config's frames, 1024 channels,
+    16 heads): (a) vggt_sparse.project_qkv (tcgen05 GEMM with q/k LayerNorm,
+    RoPE-2D, the layout split and the estimator's block means in the
+    epilogue) then SparseGlobalLayer.forward_projected (selection from the
+    means, attention); (b) the reference's composition: the qkv Linear
+    (cuBLAS bf16), LayerNorm and RoPE in PyTorch (fp32, as CUDA autocast runs
+    them), the layout gathers, then SparseGlobalLayer (estimator pooling Q and
+    K again, selection, attention).  Random-init weights, synthetic x."""
+    import vggt_sparse
+    from vggt_sparse.configs import CONFIGS
+    cfg = CONFIGS[args.config]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    heads, dim, gh, spf = 16, 1024, 37, 5
+    tpf = spf + gh * gh
+    n = cfg.frames * tpf
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(n, dim, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3 * dim, dim, device=dev, generator=g) * 0.03).to(torch.bfloat16)
+    b = (torch.randn(3 * dim, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    qn = torch.nn.LayerNorm(64).to(dev)
+    kn = torch.nn.LayerNorm(64).to(dev)
+    yy, xx = torch.meshgrid(torch.arange(gh, device=dev), torch.arange(gh, device=dev),
+                            indexing="ij")
+    grid = torch.stack((yy.flatten() + 1, xx.flatten() + 1), -1)
+    pos = torch.cat((torch.zeros(spf, 2, dtype=torch.long, device=dev), grid)).repeat(
+        cfg.frames, 1)
+    cos, sin = vggt_sparse.rope_tables(int(pos.max()) + 1, 100.0, dev)
+    fr = torch.arange(cfg.frames, device=dev)[:, None] * tpf
+    patches = (fr + spf + torch.arange(tpf - spf, device=dev)[None]).reshape(-1)
+    specials = (fr + torch.arange(spf, device=dev)[None]).reshape(-1)
+    kw = dict(mode=cfg.mode, retention=cfg.retention, tau=cfg.tau, dense_heads=cfg.dense_heads)
+    fused, sep = vggt_sparse.SparseGlobalLayer(16, **kw), vggt_sparse.SparseGlobalLayer(16, **kw)
+    if cfg.mode == "topk":
+        shape = vggt_sparse.LayerShape(frames=cfg.frames)
+        fused.topk = sep.topk = vggt_sparse.topk_budget(cfg.retention, shape.n_tokens,
+                                                        shape.n_special, shape.n_blocks, 64)
+
+    def rope(t):
+        c2 = torch.cat((cos, cos), -1)
+        s2 = torch.cat((sin, sin), -1)
+        out = []
+        for half, axis in ((t[..., :32], 0), (t[..., 32:], 1)):
+            p_ = pos[:, axis]
+            rot = torch.cat((-half[..., 16:], half[..., :16]), -1)
+            out.append(half * c2[p_] + rot * s2[p_])
+        return torch.cat(out, -1)
+
+    def unfused():
+        qkv = torch.nn.functional.linear(x, w, b).reshape(n, 3, heads, 64).permute(1, 2, 0, 3)
+        q, k, v = qkv.unbind(0)
+        q, k = rope(qn(q.float())), rope(kn(k.float()))
+        q, k, v = q.to(torch.bfloat16).contiguous(), k.to(torch.bfloat16), v
+        kp, vp = k[:, patches].contiguous(), v[:, patches].contiguous()
+        ks, vs = k[:, specials].contiguous(), v[:, specials].contiguous()
+        return sep(q, kp, vp, ks, vs)
+
+    def fusedf():
+        out = vggt_sparse.project_qkv(x, w, b, heads=heads, tokens_per_frame=tpf, q_norm=qn,
+                                      k_norm=kn, pos=pos)
+        return fused.forward_projected(out)
+
+    def proj_only():
+        return vggt_sparse.project_qkv(x, w, b, heads=heads, tokens_per_frame=tpf, q_norm=qn,
+                                       k_norm=kn, pos=pos)
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+
+    def timeit(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+    with torch.no_grad():
+        a, b_ = fusedf(), unfused()
+        torch.cuda.synchronize()
+        same = (fused.last_masks[0] == sep.last_masks[0]).all(-1).float().mean().item()
+        diff = (a.float() - b_.float()).abs()
+        t_f, t_u, t_p = timeit(fusedf), timeit(unfused), timeit(proj_only)
+    gemm_flops = 2.0 * n * dim * 3 * dim
+    peaks = load_peaks()
+    print(json.dumps({
+        "component": "qkv", "unit": "ms", "config": cfg.name,
+        "workload": "%s layer from x [%d, %d]: qkv projection (16 heads x 64), q/k LayerNorm, "
+                    "RoPE-2D, layout split, estimator, attention" % (cfg.name, n, dim),
+        "fused_layer_ms": t_f, "unfused_layer_ms": t_u, "saved_ms": t_u - t_f,
+        "fused_projection_ms": t_p,
+        "projection_tflops": gemm_flops / t_p / 1e9,
+        "projection_frac_of_peak": gemm_flops / t_p / 1e9 / peaks["bf16_tflops"],
+        "masks_equal_rows": same, "max_abs_out_diff": diff.max().item(),
+        "mean_rel_out_diff": (diff.mean() / b_.float().abs().mean()).item(),
+        "steps": args.steps, "warmup": args.warmup}), flush=True)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args)
@@ -848,6 +953,10 @@ def main():
     if args.component == "aggregator":
         if rank == 0:
             run_aggregator_bench(args)
+        return
+    if args.component == "qkv":
+        if rank == 0:
+            run_qkv_bench(args)
         return
     import vggt_sparse
     from vggt_sparse import ops

@@ -291,6 +291,49 @@ int vggt_block_mask_estimate_noalloc(const void* q, const void* patch_k, int dty
                                      float* scores, int32_t* status, void* stream);
 
 /*
+ * QKV projection with the estimator's pooling fused into its epilogue.
+ * Replaces the steps of saf3r/patch/adaptive_block_value.py:297-315 before
+ * the estimator: the `qkv` Linear (x [n_tokens, C] times w_qkv [3C, C]^T plus
+ * b_qkv [3C], C = 64 * heads, output rounded to the input dtype), q_norm /
+ * k_norm (LayerNorm over each head's 64 dims with weight / bias [64] fp32 and
+ * ln_eps; NULL for none), RoPE-2D of q and k (saf3r/models/official_vggt/
+ * layers/rope.py; pos [n_tokens, 2] int32 (y, x) and cos / sin tables
+ * [pos_count, 16] fp32 of position * base^(-i/16); pos NULL for none), the
+ * token layout's split (tokens_per_frame tokens per frame, the first
+ * special_per_frame of each special) into q [heads, n_tokens, 64],
+ * patch_k / patch_v [heads, n_patch, 64], special_k / special_v
+ * [heads, n_special, 64], and the estimator's block means
+ * (adaptive_block_value.py:16-23): pooled_q [heads, ceil(n_tokens/64), 64] and
+ * pooled_k [heads, ceil(n_patch/64), 64] fp32 (either may be NULL; pooled_k
+ * needs a workspace of vggt_qkv_workspace_size() bytes).  The means are
+ * computed in a fixed order (deterministic).
+ */
+size_t vggt_qkv_workspace_size(int64_t n_tokens, int heads);
+int vggt_qkv_project_pool(const void* x, const void* w_qkv, const void* b_qkv, int dtype,
+                          int64_t n_tokens, int heads, int tokens_per_frame,
+                          int special_per_frame, const float* q_norm_w, const float* q_norm_b,
+                          const float* k_norm_w, const float* k_norm_b, float ln_eps,
+                          const int32_t* pos, const float* rope_cos, const float* rope_sin,
+                          int pos_count, void* q, void* patch_k, void* patch_v,
+                          void* special_k, void* special_v, float* pooled_q, float* pooled_k,
+                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          void* stream);
+
+/*
+ * Scores + selection from block means of every head (e.g. the output of
+ * vggt_qkv_project_pool): slot s uses head head_ids[s] of pooled_q
+ * [pooled_heads, n_qblocks, dim] and pooled_k [pooled_heads, n_blocks, dim].
+ * Outputs and rules are those of vggt_block_mask_estimate.  A head id
+ * outside [0, pooled_heads) leaves its rows empty and sets
+ * VGGT_STATUS_BAD_HEAD.
+ */
+int vggt_block_select_pooled(const float* pooled_q, const float* pooled_k, int64_t pooled_heads,
+                             const int32_t* head_ids, int64_t n_slots, int64_t n_qblocks,
+                             int64_t n_blocks, int dim, int mode, int64_t topk, double tau,
+                             float scale, int32_t* indices, int64_t max_blocks, int32_t* counts,
+                             float* scores, int32_t* status, void* stream);
+
+/*
  * Selection only, from caller-supplied fp32 pooled scores [rows, n_blocks]
  * (row-major).  Used to re-run the selection rule on exported scores.
  */

@@ -29,5 +29,6 @@ from .attention import block_sparse_attention, dense_attention  # noqa: F401
 from .estimator import (block_mean, pooled_scores, select_mass, select_topk,  # noqa: F401
                         estimate_masks, mass_weights, topk_budget, score_keys)
 from .layout import token_layout  # noqa: F401
+from .qkv import project_qkv  # noqa: F401
 from .token_attention import token_sparse_attention  # noqa: F401
 from .frame_topk import qk_topk_per_frame, score_keys32  # noqa: F401

@@ -378,6 +378,120 @@ int vggt_block_mask_estimate(const void* q, const void* patch_k, int dtype, int6
                                            topk, tau_num, indices, max_blocks, counts, scores, s));
 }
 
+size_t vggt_qkv_workspace_size(int64_t n_tokens, int heads) {
+  if (n_tokens <= 0 || heads <= 0) return 0;
+  return vggt::qkv_pool_partial_bytes(n_tokens, heads);
+}
+
+int vggt_qkv_project_pool(const void* x, const void* w_qkv, const void* b_qkv, int dtype,
+                          int64_t n_tokens, int heads, int tokens_per_frame,
+                          int special_per_frame, const float* q_norm_w, const float* q_norm_b,
+                          const float* k_norm_w, const float* k_norm_b, float ln_eps,
+                          const int32_t* pos, const float* rope_cos, const float* rope_sin,
+                          int pos_count, void* q, void* patch_k, void* patch_v,
+                          void* special_k, void* special_v, float* pooled_q, float* pooled_k,
+                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          void* stream) {
+  g_err[0] = '\0';
+  if (dtype != VGGT_DTYPE_BF16 && dtype != VGGT_DTYPE_FP16)
+    return fail("QKV projection takes BF16 or FP16 (dtype code %d)", dtype);
+  if (heads < 1 || heads > 64) return fail("heads must be in [1, 64] (head dim 64)");
+  if (n_tokens < 0) return fail("negative n_tokens");
+  if (tokens_per_frame < 1 || special_per_frame < 0 || special_per_frame >= tokens_per_frame)
+    return fail("need tokens_per_frame >= 1 and 0 <= special_per_frame < tokens_per_frame");
+  if (n_tokens % tokens_per_frame != 0)
+    return fail("n_tokens %lld is not a whole number of %d-token frames", (long long)n_tokens,
+                tokens_per_frame);
+  if (n_tokens > 0x7fffffffLL) return fail("n_tokens exceeds 2^31 - 1");
+  if ((q_norm_w == nullptr) != (q_norm_b == nullptr) ||
+      (k_norm_w == nullptr) != (k_norm_b == nullptr))
+    return fail("LayerNorm weight and bias come together (both or neither)");
+  if (!std::isfinite(ln_eps) || ln_eps < 0.f) return fail("ln_eps must be finite and >= 0");
+  if (pos != nullptr && (rope_cos == nullptr || rope_sin == nullptr || pos_count < 1))
+    return fail("RoPE needs rope_cos / rope_sin tables with pos_count >= 1");
+  if (!vggt::qkv_pool_supported(pos != nullptr ? pos_count : 0))
+    return fail("pos_count %d: the RoPE tables do not fit shared memory", pos_count);
+  if (n_tokens == 0) return 0;
+  if (!x || !w_qkv || !q || !patch_k || !patch_v ||
+      (special_per_frame > 0 && (!special_k || !special_v)))
+    return fail("x, w_qkv and the q / k / v outputs must be non-NULL");
+  const int64_t c = (int64_t)heads * 64;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(x) || !a16(w_qkv) || !a16(q) || !a16(patch_k) || !a16(patch_v) ||
+      (special_per_frame > 0 && (!a16(special_k) || !a16(special_v))) ||
+      (b_qkv != nullptr && (reinterpret_cast<uintptr_t>(b_qkv) & 3u)))
+    return fail("x, w_qkv and the outputs must be 16-byte aligned (bias 4-byte)");
+  (void)c;
+  const size_t need = vggt::qkv_pool_partial_bytes(n_tokens, heads);
+  if (pooled_k != nullptr) {
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail("pooled_k needs a workspace of %zu bytes", need);
+    if (!a16(workspace)) return fail("workspace must be 16-byte aligned");
+  }
+  vggt::QkvPoolArgs a;
+  a.x = x;
+  a.w = w_qkv;
+  a.bias = b_qkv;
+  a.qn_w = q_norm_w;
+  a.qn_b = q_norm_b;
+  a.kn_w = k_norm_w;
+  a.kn_b = k_norm_b;
+  a.pos = pos;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.pos_count = pos_count;
+  a.ln_eps = ln_eps;
+  a.q = q;
+  a.kp = patch_k;
+  a.vp = patch_v;
+  a.ks = special_k;
+  a.vs = special_v;
+  a.pooled_q = pooled_q;
+  a.pooled_k = pooled_k;
+  a.workspace = workspace;
+  a.status = status;
+  a.n_tokens = n_tokens;
+  a.heads = heads;
+  a.dtype = dtype;
+  a.tok_per_frame = tokens_per_frame;
+  a.special_per_frame = special_per_frame;
+  return cuda_rc(vggt::launch_qkv_pool(a, static_cast<cudaStream_t>(stream)));
+}
+
+int vggt_block_select_pooled(const float* pooled_q, const float* pooled_k, int64_t pooled_heads,
+                             const int32_t* head_ids, int64_t n_slots, int64_t n_qblocks,
+                             int64_t n_blocks, int dim, int mode, int64_t topk, double tau,
+                             float scale, int32_t* indices, int64_t max_blocks, int32_t* counts,
+                             float* scores, int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (dim != 32 && dim != 64) return fail("head dim %d unsupported (32 or 64)", dim);
+  if (pooled_heads < 1 || n_slots < 0 || n_qblocks < 0 || n_blocks < 1)
+    return fail("invalid sizes (need pooled_heads >= 1, n_blocks >= 1)");
+  if (n_slots > 65535) return fail("n_slots %lld exceeds 65535", (long long)n_slots);
+  if (!std::isfinite(scale)) return fail("scale must be finite");
+  if (n_blocks > vggt::estimator_max_blocks_supported(dim))
+    return fail("%lld key blocks exceed the supported maximum", (long long)n_blocks);
+  uint64_t tau_num = 0;
+  if (mode == VGGT_SELECT_TOPK) {
+    if (topk < 1) return fail("topk must be >= 1");
+    if (max_blocks < std::min<int64_t>(topk, n_blocks)) return fail("max_blocks too small");
+  } else if (mode == VGGT_SELECT_MASS) {
+    if (!(tau > 0.0 && tau <= 1.0)) return fail("tau must be in (0, 1]");
+    if (max_blocks < n_blocks) return fail("max_blocks too small");
+    tau_num = (uint64_t)std::floor(tau * (double)(1ull << vggt::kTauBits) + 0.5);
+    if (tau_num == 0) tau_num = 1;
+  } else {
+    return fail("unknown selection mode %d", mode);
+  }
+  if (n_slots == 0 || n_qblocks == 0) return 0;
+  if (!pooled_q || !pooled_k || !head_ids || !indices || !counts)
+    return fail("pooled_q, pooled_k, head_ids, indices and counts must be non-NULL");
+  return cuda_rc(vggt::launch_score_select_mapped(
+      pooled_q, pooled_k, dim, n_qblocks, n_blocks, head_ids, pooled_heads, n_slots, scale, mode,
+      topk, tau_num, indices, max_blocks, counts, scores, status,
+      static_cast<cudaStream_t>(stream)));
+}
+
 int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int mode, int64_t topk,
                       double tau, int32_t* indices, int64_t max_blocks, int32_t* counts,
                       void* stream) {

@@ -274,7 +274,8 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
     const float* __restrict__ pooled_q, const float* __restrict__ pooled_k, int64_t qb_count,
     int64_t nb, float scale, int mode, int64_t topk, uint64_t tau_num,
     int32_t* __restrict__ indices, int64_t max_blocks, int32_t* __restrict__ counts,
-    float* __restrict__ scores_out, const float* __restrict__ scores_in) {
+    float* __restrict__ scores_out, const float* __restrict__ scores_in,
+    const int32_t* __restrict__ head_map, int64_t pooled_heads, int32_t* __restrict__ status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SelectHist* hist = reinterpret_cast<SelectHist*>(smem_raw);                // [8]
   float* qbar = reinterpret_cast<float*>(hist + 8);
@@ -292,11 +293,26 @@ __global__ void __launch_bounds__(256, 3) score_select_kernel(
       for (int64_t i = tid; i < nb; i += blockDim.x) srows[r * nb + i] = src[i];
     }
   } else {
-    const float* qsrc = pooled_q + (slot * qb_count + r0) * D;
+    // pooled rows of this slot's head (with head_map: means of every head,
+    // the slot picking its head)
+    int64_t src = slot;
+    if (head_map != nullptr) {
+      src = head_map[slot];
+      if (src < 0 || src >= pooled_heads) {
+        if (tid == 0 && status) atomicOr(status, VGGT_STATUS_BAD_HEAD);
+        for (int r = 0; r < rows; ++r) {
+          const int64_t row = slot * qb_count + r0 + r;
+          for (int64_t j = tid; j < max_blocks; j += blockDim.x) indices[row * max_blocks + j] = -1;
+          if (tid == 0) counts[row] = 0;
+        }
+        return;
+      }
+    }
+    const float* qsrc = pooled_q + (src * qb_count + r0) * D;
     for (int i = tid; i < rows * D; i += blockDim.x) qbar[i] = qsrc[i];
     for (int i = rows * D + tid; i < RMAX * D; i += blockDim.x) qbar[i] = 0.f;
     __syncthreads();
-    const float* ksrc = pooled_k + slot * nb * D;
+    const float* ksrc = pooled_k + src * nb * D;
     for (int64_t kb = tid; kb < nb; kb += blockDim.x) {
       // every row's dot product accumulates d = 0 .. D-1 in order (one fmaf
       // each); pooled K is streamed in 16-float chunks to keep registers low
@@ -359,6 +375,7 @@ static cudaError_t launch_select_r(const float* pq, const float* pk, int64_t qb_
                                    int64_t n_slots, float scale, int mode, int64_t topk,
                                    uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                    int32_t* counts, float* scores_out, const float* scores_in,
+                                   const int32_t* head_map, int64_t pooled_heads, int32_t* status,
                                    cudaStream_t stream) {
   const size_t smem = select_smem_bytes(RMAX, nb, D, FROM);
   auto kern = score_select_kernel<D, FROM, RMAX>;
@@ -367,7 +384,8 @@ static cudaError_t launch_select_r(const float* pq, const float* pk, int64_t qb_
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((qb_count + RMAX - 1) / RMAX), (unsigned)n_slots);
   kern<<<grid, 256, smem, stream>>>(pq, pk, qb_count, nb, scale, mode, topk, tau_num, indices,
-                                     max_blocks, counts, scores_out, scores_in);
+                                     max_blocks, counts, scores_out, scores_in, head_map,
+                                     pooled_heads, status);
   return cudaGetLastError();
 }
 
@@ -378,13 +396,16 @@ static cudaError_t launch_select_t(const float* pq, const float* pk, int64_t qb_
                                    int64_t n_slots, float scale, int mode, int64_t topk,
                                    uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                    int32_t* counts, float* scores_out, const float* scores_in,
-                                   cudaStream_t stream) {
+                                   cudaStream_t stream, const int32_t* head_map = nullptr,
+                                   int64_t pooled_heads = 0, int32_t* status = nullptr) {
   if (select_smem_bytes(8, nb, D, FROM) <= kSelectSmemBudget)
     return launch_select_r<D, FROM, 8>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
-                                       indices, max_blocks, counts, scores_out, scores_in, stream);
+                                       indices, max_blocks, counts, scores_out, scores_in,
+                                       head_map, pooled_heads, status, stream);
   if (select_smem_bytes(2, nb, D, FROM) <= kSelectSmemBudget)
     return launch_select_r<D, FROM, 2>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
-                                       indices, max_blocks, counts, scores_out, scores_in, stream);
+                                       indices, max_blocks, counts, scores_out, scores_in,
+                                       head_map, pooled_heads, status, stream);
   return cudaErrorInvalidValue;
 }
 
@@ -430,6 +451,22 @@ cudaError_t launch_score_select(const float* pq, const float* pk, int d, int64_t
                                       indices, max_blocks, counts, scores_out, nullptr, stream);
   return launch_select_t<32, false>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
                                     indices, max_blocks, counts, scores_out, nullptr, stream);
+}
+
+cudaError_t launch_score_select_mapped(const float* pq, const float* pk, int d, int64_t qb_count,
+                                       int64_t nb, const int32_t* head_map, int64_t pooled_heads,
+                                       int64_t n_slots, float scale, int mode, int64_t topk,
+                                       uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                       int32_t* counts, float* scores_out, int32_t* status,
+                                       cudaStream_t stream) {
+  if (units_zero(n_slots, qb_count)) return cudaSuccess;
+  if (d == 64)
+    return launch_select_t<64, false>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                      indices, max_blocks, counts, scores_out, nullptr, stream,
+                                      head_map, pooled_heads, status);
+  return launch_select_t<32, false>(pq, pk, qb_count, nb, n_slots, scale, mode, topk, tau_num,
+                                    indices, max_blocks, counts, scores_out, nullptr, stream,
+                                    head_map, pooled_heads, status);
 }
 
 cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int64_t nb, int mode,

@@ -16,6 +16,14 @@ cudaError_t launch_score_select(const float* pq, const float* pk, int d, int64_t
                                 int64_t nb, int64_t n_slots, float scale, int mode, int64_t topk,
                                 uint64_t tau_num, int32_t* indices, int64_t max_blocks,
                                 int32_t* counts, float* scores_out, cudaStream_t stream);
+// scores + selection from block means of every head: slot s reads head
+// head_map[s] of [pooled_heads, ...] (out-of-range heads: BAD_HEAD, empty rows)
+cudaError_t launch_score_select_mapped(const float* pq, const float* pk, int d, int64_t qb_count,
+                                       int64_t nb, const int32_t* head_map, int64_t pooled_heads,
+                                       int64_t n_slots, float scale, int mode, int64_t topk,
+                                       uint64_t tau_num, int32_t* indices, int64_t max_blocks,
+                                       int32_t* counts, float* scores_out, int32_t* status,
+                                       cudaStream_t stream);
 cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int64_t nb, int mode,
                                       int64_t topk, uint64_t tau_num, int32_t* indices,
                                       int64_t max_blocks, int32_t* counts, cudaStream_t stream);
@@ -110,6 +118,35 @@ struct FrameTopkArgs {
 bool frame_topk_supported(int dim, int64_t topk);
 int64_t frame_topk_groups(int64_t frames, int64_t work_rows);
 cudaError_t launch_frame_topk(const FrameTopkArgs& a, cudaStream_t stream);
+// qkv_pool.cu: QKV projection + q/k LayerNorm + RoPE-2D + layout split + block means
+struct QkvPoolArgs {
+  const void* x;        // [n_tokens, heads * 64]
+  const void* w;        // [3 * heads * 64, heads * 64] (nn.Linear weight)
+  const void* bias;     // [3 * heads * 64] or null
+  const float* qn_w;    // [64] or null
+  const float* qn_b;
+  const float* kn_w;
+  const float* kn_b;
+  const int32_t* pos;   // [n_tokens, 2] or null (no RoPE)
+  const float* rope_cos;  // [pos_count, 16]
+  const float* rope_sin;
+  int pos_count;
+  float ln_eps;
+  void* q;              // [heads, n_tokens, 64]
+  void* kp;
+  void* vp;
+  void* ks;
+  void* vs;
+  float* pooled_q;      // [heads, ceil(n_tokens / 64), 64] or null
+  float* pooled_k;      // [heads, ceil(n_patch / 64), 64] or null
+  void* workspace;      // qkv_pool_partial_bytes when pooled_k is set
+  int32_t* status;
+  int64_t n_tokens;
+  int heads, dtype, tok_per_frame, special_per_frame;
+};
+size_t qkv_pool_partial_bytes(int64_t n_tokens, int heads);
+bool qkv_pool_supported(int pos_count);
+cudaError_t launch_qkv_pool(const QkvPoolArgs& a, cudaStream_t stream);
 // attn_mma.cu
 cudaError_t launch_attn_mma(const AttnArgs& a, cudaStream_t stream);
 // attn_tc05.cu

@@ -1,0 +1,556 @@
+// QKV projection with the estimator's block pooling in its epilogue.
+//
+// Computes what saf3r/patch/adaptive_block_value.py:297-315 computes before
+// the estimator: qkv = x W^T + b (the module's `qkv` Linear, output rounded
+// to the input dtype), q_norm / k_norm (LayerNorm over the 64 dims of a head,
+// fp32), RoPE-2D (saf3r/models/official_vggt/layers/rope.py: the first 32
+// dims rotate with the token's y position, the last 32 with its x position;
+// the caller passes the cos / sin tables), q and k rounded back to the input
+// dtype, the token layout's patch / special split
+// (saf3r/patch/value_evolving_attention.py:17-20), and the block means the
+// estimator pools (adaptive_block_value.py:16-23 block_mean) over 64-token
+// query blocks of q and 64-row blocks of the patch keys.
+//
+// One work tile = 128 token rows x one head: a tcgen05 GEMM of M=128, N=192
+// (the head's 64 q, 64 k and 64 v rows of W, three TMA boxes per K step),
+// K = model dim in steps of 64 through a 3-stage TMA ring, fp32 accumulator
+// in TMEM.  CTAs are persistent (one per SM) with two TMEM accumulators, so
+// the epilogue of one tile (warps 2-5, one token row per thread) overlaps the
+// MMAs of the next.  A thread holds a whole head row, so LayerNorm and RoPE
+// need no cross-thread traffic; block sums go through a shared-memory
+// transpose in a fixed order (deterministic).  Query blocks never straddle
+// tiles (128 = 2 x 64 rows); patch-key blocks can, so each tile writes its
+// partial sums of the (at most three) patch blocks it touches and a second,
+// small kernel folds a block's partials in tile order.
+//
+// Every wait is bounded (1 s); on expiry the CTA raises an abort flag, sets
+// VGGT_STATUS_TIMEOUT, drains its copies and MMAs, frees TMEM and exits.
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc05.cuh"
+
+namespace vggt {
+
+namespace qkvp {
+
+constexpr int BM = 128;     // token rows per tile
+constexpr int HD = 64;      // head dim
+constexpr int BK = 64;      // K per stage
+constexpr int NO = 3 * HD;  // MMA N: q | k | v of one head
+constexpr int NST = 3;
+constexpr int THREADS = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
+constexpr uint32_t B_BYTES = NO * BK * 2;  // 24 KB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = 512;        // two accumulators of 192 in 256-column slots
+constexpr uint64_t LIMIT_NS = 1000000000ull;
+constexpr int TPITCH = HD + 1;             // transpose buffer row pitch (floats)
+
+constexpr uint32_t OFF_STAGE = 0;
+constexpr uint32_t OFF_T = NST * STAGE_BYTES;          // float[BM][TPITCH]
+constexpr uint32_t OFF_ROW = OFF_T + BM * TPITCH * 4;  // int[BM]: patch block of each row
+constexpr uint32_t OFF_BAR = (OFF_ROW + BM * 4 + 7) & ~7u;
+constexpr int B_FULL = 0;                 // [NST]
+constexpr int B_EMPTY = B_FULL + NST;     // [NST]
+constexpr int B_ACCFULL = B_EMPTY + NST;  // [2]
+constexpr int B_ACCEMPTY = B_ACCFULL + 2; // [2]
+constexpr int B_DRAIN = B_ACCEMPTY + 2;
+constexpr int NBAR = B_DRAIN + 1;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;           // tmem base, abort flag, votes
+constexpr uint32_t OFF_ROPE = (OFF_MISC + 32 + 15) & ~15u;  // float2[pos_count][16] (cos, sin)
+
+struct Params {
+  const void* bias;     // [3C] in x's dtype, or null
+  const float* qn_w;    // [64] LayerNorm weight / bias of q, or null (no q_norm)
+  const float* qn_b;
+  const float* kn_w;    // [64] of k, or null
+  const float* kn_b;
+  const int32_t* pos;   // [N, 2] (y, x) token positions, or null (no RoPE)
+  const float* rope_cos;  // [pos_count, 16]
+  const float* rope_sin;
+  void* q;              // [H, N, 64]
+  void* kp;             // [H, NP, 64]
+  void* vp;
+  void* ks;             // [H, NS, 64]
+  void* vs;
+  float* pooled_q;      // [H, QB, 64] means, or null
+  float* part_k;        // [row tiles, H, 3, 64] partial sums of patch-key blocks, or null
+  int32_t* part_blk;    // [row tiles, H, 3] their block ids (-1 unused)
+  int32_t* status;
+  int64_t n, n_patch, n_special, qb_count;
+  int heads, k_steps;   // model dim / 64
+  int tok_per_frame, special_per_frame;
+  int pos_count;        // rows of the RoPE tables (largest position + 1)
+  float ln_eps;
+  int64_t tiles;        // row tiles x heads
+};
+
+template <typename T>
+__device__ __forceinline__ float round_t(float v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return __bfloat162float(__float2bfloat16_rn(v));
+  else
+    return __half2float(__float2half_rn(v));
+}
+
+// patch index of a token, or -1 for a special token
+__device__ __forceinline__ int64_t patch_of(int64_t t, const Params& p) {
+  const int64_t f = t / p.tok_per_frame;
+  const int64_t j = t - f * p.tok_per_frame;
+  if (j < p.special_per_frame) return -1;
+  return f * (p.tok_per_frame - p.special_per_frame) + (j - p.special_per_frame);
+}
+
+// LayerNorm (biased variance, like torch.nn.LayerNorm) and RoPE-2D of one
+// head row held by the thread.  The rotation is x cos + rotate(x) sin with
+// rotate(a, b) = (-b, a) over each 32-dim half, as separately rounded fp32
+// products and sum.
+__device__ __forceinline__ void norm_rope(float* v, const float* w, const float* b, float eps,
+                                          bool rope, int py, int px, const float2* table) {
+  if (w != nullptr) {
+    // eight interleaved partial sums keep the dependent chains short
+    float s8[8], q8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s8[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) s8[i & 7] += v[i];
+    const float mean =
+        (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))) * (1.f / HD);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; ++i) {
+      const float d = v[i] - mean;
+      q8[i & 7] = fmaf(d, d, q8[i & 7]);
+    }
+    const float q =
+        ((q8[0] + q8[1]) + (q8[2] + q8[3])) + ((q8[4] + q8[5]) + (q8[6] + q8[7]));
+    const float rstd = rsqrtf(q * (1.f / HD) + eps);
+#pragma unroll
+    for (int i = 0; i < HD; ++i) v[i] = fmaf((v[i] - mean) * rstd, __ldg(w + i), __ldg(b + i));
+  }
+  if (rope) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const float2* cs = table + (half ? px : py) * 16;
+      float* u = v + 32 * half;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 c = cs[i];
+        const float a = u[i], bb = u[i + 16];
+        u[i] = __fadd_rn(__fmul_rn(a, c.x), __fmul_rn(-bb, c.y));
+        u[i + 16] = __fadd_rn(__fmul_rn(bb, c.x), __fmul_rn(a, c.y));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 64 consecutive values as 8 16-byte stores
+template <typename T>
+__device__ __forceinline__ void store_row(T* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint4 w;
+    w.x = ElemOps<T>::pack2(v[8 * q + 0], v[8 * q + 1]);
+    w.y = ElemOps<T>::pack2(v[8 * q + 2], v[8 * q + 3]);
+    w.z = ElemOps<T>::pack2(v[8 * q + 4], v[8 * q + 5]);
+    w.w = ElemOps<T>::pack2(v[8 * q + 6], v[8 * q + 7]);
+    d[q] = w;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 1)
+    qkv_pool_kernel(const __grid_constant__ CUtensorMap tm_x,
+                    const __grid_constant__ CUtensorMap tm_w, Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  unsigned char* sbase = smem_raw + (base - raw_addr);
+  const uint32_t bar0 = base + OFF_BAR;
+  auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
+  float* tbuf = reinterpret_cast<float*>(sbase + OFF_T);
+  int* rowblk = reinterpret_cast<int*>(sbase + OFF_ROW);
+  float2* table = reinterpret_cast<float2*>(sbase + OFF_ROPE);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t H = p.heads;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc::mbar_init(bar(B_FULL + s), 1);
+      tc::mbar_init(bar(B_EMPTY + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(bar(B_ACCFULL + b), 1);
+      tc::mbar_init(bar(B_ACCEMPTY + b), 128);
+    }
+    tc::mbar_init(bar(B_DRAIN), 1);
+    misc[1] = 0u;
+    tc::mbar_fence_init();
+  }
+  if (p.pos != nullptr)
+    for (int e = tid; e < p.pos_count * 16; e += THREADS)
+      table[e] = make_float2(p.rope_cos[e], p.rope_sin[e]);
+  if (warp == 1) {
+    tc::tmem_alloc(base + OFF_MISC, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_x);
+      tc::prefetch_tmap(&tm_w);
+      int64_t it = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.tiles; u += gridDim.x) {
+        const int rt = (int)(u / H), h = (int)(u % H);
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = (int)(it % NST);
+          if (it >= NST &&
+              !tc::mbar_wait(bar(B_EMPTY + s), (uint32_t)((it / NST - 1) & 1), abort_flag,
+                             LIMIT_NS)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = base + OFF_STAGE + (uint32_t)s * STAGE_BYTES;
+          tc::mbar_expect_tx(bar(B_FULL + s), STAGE_BYTES);
+          tc::tma_load_3d(dst, &tm_x, bar(B_FULL + s), k * BK, rt * BM, 0);
+          const int c = p.heads * HD;  // model dim
+#pragma unroll
+          for (int j = 0; j < 3; ++j)
+            tc::tma_load_3d(dst + A_BYTES + (uint32_t)j * (HD * BK * 2), &tm_w, bar(B_FULL + s),
+                            k * BK, j * c + h * HD, 0);
+        }
+      }
+      // drain: the last NST stages' copies, landed or not
+      for (int64_t t = it > NST ? it - NST : 0; t < it; ++t)
+        tc::mbar_wait_drain(bar(B_FULL + (int)(t % NST)), (uint32_t)((t / NST) & 1), LIMIT_NS);
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc = tc::idesc_f16(fmt, 0u, BM, NO);
+      int64_t it = 0, i = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.tiles; u += gridDim.x, ++i) {
+        const int b = (int)(i & 1);
+        // the epilogue must have read accumulator b (tile i - 2) out
+        if (i >= 2 && !tc::mbar_wait(bar(B_ACCEMPTY + b), (uint32_t)(((i >> 1) + 1) & 1),
+                                     abort_flag, LIMIT_NS)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)b * 256u;
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = (int)(it % NST);
+          if (!tc::mbar_wait(bar(B_FULL + s), (uint32_t)((it / NST) & 1), abort_flag, LIMIT_NS)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = base + OFF_STAGE + (uint32_t)s * STAGE_BYTES;
+          const uint64_t adesc = tc::sw128_desc(a_addr, 16);
+          const uint64_t bdesc = tc::sw128_desc(a_addr + A_BYTES, 16);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::mma_ss(acc, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                       (k > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_commit(bar(B_EMPTY + s));
+        }
+        if (ok) tc::mma_commit(bar(B_ACCFULL + b));
+      }
+      tc::mma_commit(bar(B_DRAIN));
+      tc::mbar_wait_drain(bar(B_DRAIN), 0, LIMIT_NS);
+    }
+  } else {
+    // ================= epilogue: warps 2-5, one token row per thread =================
+    const int sub = warp & 3;          // TMEM lane quarter of this warp
+    const int row = sub * 32 + lane;   // 0..127
+    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    const bool rope = p.pos != nullptr;
+    volatile int* vote = reinterpret_cast<volatile int*>(misc + 4);  // one flag per warp
+    int64_t i = 0;
+    for (int64_t u = blockIdx.x; u < p.tiles; u += gridDim.x, ++i) {
+      const int b = (int)(i & 1);
+      const int64_t rt = u / H;
+      const int h = (int)(u % H);
+      const bool got = tc::mbar_wait(bar(B_ACCFULL + b), (uint32_t)((i >> 1) & 1), abort_flag,
+                                     LIMIT_NS);
+      // the four warps leave together (the named barriers below are not
+      // bounded, so no warp may stop at one the others never reach)
+      const bool warp_ok = __all_sync(0xffffffffu, got);
+      if (lane == 0) vote[sub] = warp_ok ? 1 : 0;
+      epi_sync();
+      const bool all_ok = vote[0] && vote[1] && vote[2] && vote[3];
+      epi_sync();
+      if (!all_ok) break;
+      tc::tc_fence_after();
+      const uint32_t acc = tmem + (uint32_t)b * 256u + lane_off;
+      const int64_t t = rt * BM + row;
+      const bool valid = t < p.n;
+      const int64_t pidx = valid ? patch_of(t, p) : -1;
+      int py = 0, px = 0;
+      if (rope && valid) {
+        py = p.pos[2 * t];
+        px = p.pos[2 * t + 1];
+        py = py < 0 ? 0 : (py >= p.pos_count ? p.pos_count - 1 : py);
+        px = px < 0 ? 0 : (px >= p.pos_count ? p.pos_count - 1 : px);
+      }
+      const T* bias = static_cast<const T*>(p.bias);
+      float v[HD];
+#pragma unroll
+      for (int part = 0; part < 3; ++part) {
+        // accumulator columns [64 part, 64 part + 64): q, k, v of head h
+        uint32_t r[64];
+        tc::tmem_ld32(acc + (uint32_t)(64 * part), r);
+        tc::tmem_ld32(acc + (uint32_t)(64 * part + 32), r + 32);
+        tc::tmem_wait_ld();
+        const int bcol = part * p.heads * HD + h * HD;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) v[d] = __uint_as_float(r[d]);
+        if (bias != nullptr) {
+#pragma unroll
+          for (int d = 0; d < HD; d += 2) {
+            const float2 bb = ElemOps<T>::to_float2(
+                *reinterpret_cast<const uint32_t*>(bias + bcol + d));
+            v[d] += bb.x;
+            v[d + 1] += bb.y;
+          }
+        }
+        // the Linear's output is rounded to the activation dtype
+#pragma unroll
+        for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
+        if (part < 2) {
+          norm_rope(v, part == 0 ? p.qn_w : p.kn_w, part == 0 ? p.qn_b : p.kn_b, p.ln_eps, rope,
+                    py, px, table);
+#pragma unroll
+          for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
+        }
+        if (valid) {
+          T* dst;
+          if (part == 0)
+            dst = static_cast<T*>(p.q) + (h * p.n + t) * HD;
+          else if (pidx >= 0)
+            dst = static_cast<T*>(part == 1 ? p.kp : p.vp) + (h * p.n_patch + pidx) * HD;
+          else {
+            const int64_t f = t / p.tok_per_frame;
+            const int64_t sidx = f * p.special_per_frame + (t - f * p.tok_per_frame);
+            dst = static_cast<T*>(part == 1 ? p.ks : p.vs) + (h * p.n_special + sidx) * HD;
+          }
+          store_row<T>(dst, v);
+        }
+        if (part == 0 && p.pooled_q != nullptr) {
+          // query-block means: thread (half, col) sums column col over rows
+          // [64 half, 64 half + 64) of the tile (four interleaved partial sums)
+#pragma unroll
+          for (int d = 0; d < HD; ++d) tbuf[row * TPITCH + d] = valid ? v[d] : 0.f;
+          epi_sync();
+          const int half = row >> 6, col = row & 63;
+          const int64_t qb = rt * 2 + half;
+          if (qb < p.qb_count) {
+            float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int j = 0; j < 64; ++j) a[j & 3] += tbuf[(half * 64 + j) * TPITCH + col];
+            const int64_t nrow = p.n - qb * 64 < 64 ? p.n - qb * 64 : 64;
+            p.pooled_q[(h * p.qb_count + qb) * HD + col] =
+                ((a[0] + a[1]) + (a[2] + a[3])) / (float)nrow;
+          }
+          epi_sync();
+        }
+        if (part == 1 && p.part_k != nullptr) {
+          // patch-key block partial sums over this tile's patch rows: the tile
+          // touches blocks first .. first + 2 at most (128 patch rows); thread
+          // (half, col) sums column col of its 64 rows into one accumulator per
+          // block, then the halves are added (half 0 + half 1)
+          int first = -1;
+          {
+            const int64_t t0 = rt * BM;
+            const int64_t f = t0 / p.tok_per_frame, j = t0 - f * p.tok_per_frame;
+            const int64_t tf = j < p.special_per_frame ? f * p.tok_per_frame + p.special_per_frame
+                                                       : t0;
+            if (tf < p.n && tf < t0 + BM) first = (int)(patch_of(tf, p) >> 6);
+          }
+#pragma unroll
+          for (int d = 0; d < HD; ++d) tbuf[row * TPITCH + d] = pidx >= 0 ? v[d] : 0.f;
+          rowblk[row] = pidx >= 0 ? (int)(pidx >> 6) - first : -1;  // slot 0..2, -1 none
+          epi_sync();
+          const int half = row >> 6, col = row & 63;
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+          int seen = 0;  // bit s: some row of this half falls in slot s
+#pragma unroll 4
+          for (int j = half * 64; j < half * 64 + 64; ++j) {
+            const int sl = rowblk[j];
+            const float x = tbuf[j * TPITCH + col];
+            a0 += sl == 0 ? x : 0.f;
+            a1 += sl == 1 ? x : 0.f;
+            a2 += sl == 2 ? x : 0.f;
+            seen |= sl >= 0 ? 1 << sl : 0;
+          }
+          float* kx = tbuf;  // reuse: [3][64] partials of half 1, then the seen flags
+          epi_sync();
+          if (half == 1) {
+            kx[col] = a0;
+            kx[64 + col] = a1;
+            kx[128 + col] = a2;
+            if (col == 0) rowblk[0] = seen;
+          }
+          epi_sync();
+          if (half == 0) {
+            const int64_t pbase = (rt * H + h) * 3;
+            const int both = seen | rowblk[0];
+            p.part_k[(pbase + 0) * HD + col] = a0 + kx[col];
+            p.part_k[(pbase + 1) * HD + col] = a1 + kx[64 + col];
+            p.part_k[(pbase + 2) * HD + col] = a2 + kx[128 + col];
+            if (col < 3) p.part_blk[pbase + col] = (both >> col) & 1 ? first + col : -1;
+          }
+          epi_sync();
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar(B_ACCEMPTY + b));
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag && p.status) atomicOr(p.status, VGGT_STATUS_TIMEOUT);
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Patch-key block means from the tiles' partial sums: one warp per (head,
+// block), the block's (at most two) tiles added in tile order.
+__global__ void __launch_bounds__(256)
+    fold_k_kernel(const float* __restrict__ part_k, const int32_t* __restrict__ part_blk,
+                  int64_t heads, int64_t nb, int64_t n_patch, int tok_per_frame,
+                  int special_per_frame, float* __restrict__ pooled_k) {
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (unit >= heads * nb) return;
+  const int64_t h = unit / nb, blk = unit % nb;
+  const int ppf = tok_per_frame - special_per_frame;
+  auto token_of = [&](int64_t pi) {
+    return (pi / ppf) * tok_per_frame + special_per_frame + pi % ppf;
+  };
+  const int64_t p0 = blk * 64;
+  const int64_t p1 = (blk + 1) * 64 < n_patch ? (blk + 1) * 64 - 1 : n_patch - 1;
+  const int64_t t_lo = token_of(p0) / BM, t_hi = token_of(p1) / BM;
+  float s0 = 0.f, s1 = 0.f;
+  for (int64_t rt = t_lo; rt <= t_hi; ++rt) {
+    const int64_t pbase = (rt * heads + h) * 3;
+    for (int sl = 0; sl < 3; ++sl)
+      if (part_blk[pbase + sl] == blk) {
+        s0 += part_k[(pbase + sl) * HD + lane];
+        s1 += part_k[(pbase + sl) * HD + lane + 32];
+      }
+  }
+  const float pop = (float)(p1 - p0 + 1);
+  pooled_k[(h * nb + blk) * HD + lane] = s0 / pop;
+  pooled_k[(h * nb + blk) * HD + lane + 32] = s1 / pop;
+}
+
+static size_t smem_bytes(int pos_count) {
+  return 1024 + OFF_ROPE + (size_t)pos_count * 16 * sizeof(float2);
+}
+
+}  // namespace qkvp
+
+size_t qkv_pool_partial_bytes(int64_t n_tokens, int heads) {
+  const int64_t rt = (n_tokens + qkvp::BM - 1) / qkvp::BM;
+  return (((size_t)rt * heads * 3 * qkvp::HD * 4 + 255) & ~(size_t)255) +
+         (((size_t)rt * heads * 3 * 4 + 255) & ~(size_t)255);
+}
+
+bool qkv_pool_supported(int pos_count) {
+  return pos_count >= 0 && qkvp::smem_bytes(pos_count) <= 227u * 1024u;
+}
+
+cudaError_t launch_qkv_pool(const QkvPoolArgs& a, cudaStream_t stream) {
+  using namespace qkvp;
+  if (a.n_tokens == 0) return cudaSuccess;
+  const int c = a.heads * HD;
+  CUtensorMap mx, mw;
+  if (!encode_tmap_3d_sw128(&mx, a.x, a.dtype, c, a.n_tokens, 1, BK, BM) ||
+      !encode_tmap_3d_sw128(&mw, a.w, a.dtype, c, 3 * c, 1, BK, HD))
+    return cudaErrorInvalidValue;
+  Params p;
+  p.bias = a.bias;
+  p.qn_w = a.qn_w;
+  p.qn_b = a.qn_b;
+  p.kn_w = a.kn_w;
+  p.kn_b = a.kn_b;
+  p.pos = a.pos;
+  p.rope_cos = a.rope_cos;
+  p.rope_sin = a.rope_sin;
+  p.q = a.q;
+  p.kp = a.kp;
+  p.vp = a.vp;
+  p.ks = a.ks;
+  p.vs = a.vs;
+  p.pooled_q = a.pooled_q;
+  p.status = a.status;
+  p.n = a.n_tokens;
+  p.tok_per_frame = a.tok_per_frame;
+  p.special_per_frame = a.special_per_frame;
+  const int64_t frames = a.n_tokens / a.tok_per_frame;
+  p.n_patch = frames * (a.tok_per_frame - a.special_per_frame);
+  p.n_special = frames * a.special_per_frame;
+  p.qb_count = (a.n_tokens + 63) / 64;
+  p.heads = a.heads;
+  p.k_steps = c / BK;
+  p.pos_count = a.pos != nullptr ? a.pos_count : 0;
+  p.ln_eps = a.ln_eps;
+  const int64_t rtiles = (a.n_tokens + BM - 1) / BM;
+  p.tiles = rtiles * a.heads;
+  unsigned char* ws = static_cast<unsigned char*>(a.workspace);
+  p.part_k = a.pooled_k != nullptr ? reinterpret_cast<float*>(ws) : nullptr;
+  p.part_blk = a.pooled_k != nullptr
+                   ? reinterpret_cast<int32_t*>(
+                         ws + (((size_t)rtiles * a.heads * 3 * HD * 4 + 255) & ~(size_t)255))
+                   : nullptr;
+  const size_t smem = smem_bytes(p.pos_count);
+  int sms = 0, dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = p.tiles < sms ? p.tiles : sms;
+  if (a.dtype == VGGT_DTYPE_BF16) {
+    auto k = qkv_pool_kernel<__nv_bfloat16>;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mx, mw, p);
+  } else {
+    auto k = qkv_pool_kernel<__half>;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k<<<(unsigned)grid, THREADS, smem, stream>>>(mx, mw, p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess || a.pooled_k == nullptr) return e;
+  const int64_t nb = (p.n_patch + 63) / 64;
+  const int64_t units = a.heads * nb;
+  fold_k_kernel<<<(unsigned)((units + 7) / 8), 256, 0, stream>>>(
+      p.part_k, p.part_blk, a.heads, nb, p.n_patch, a.tok_per_frame, a.special_per_frame,
+      a.pooled_k);
+  return cudaGetLastError();
+}
+
+}  // namespace vggt

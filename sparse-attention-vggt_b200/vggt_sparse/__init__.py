@@ -16,6 +16,7 @@ from .frame_topk import compute_qk_topk_indices_fused  # noqa: F401
 from .layer import SparseGlobalLayer, topk_budget  # noqa: F401
 from .layout import LayerShape, split_keys, token_layout  # noqa: F401
 from .pipeline import HostPipeline  # noqa: F401
+from .qkv import QkvOut, project_qkv, rope_tables  # noqa: F401
 from .token_attention import token_sparse_attention  # noqa: F401
 from .profile import (dense_heads_from_decisions, dense_heads_from_profile,  # noqa: F401
                       head_modes_from_profile, split_heads)

@@ -107,6 +107,27 @@ class SparseGlobalLayer:
         self.last_masks = (buf["indices"], buf["counts"])
         return buf
 
+    def estimate_pooled(self, pooled_q, pooled_k, n_tokens, n_patch, n_special):
+        """The estimator's selection from block means of every head (pooled_q
+        [H, QB, d], pooled_k [H, NB, d] fp32, e.g. from ``project_qkv``): the
+        masks of ``estimate`` without another pass over Q and K."""
+        buf = self._buffers(pooled_q.device, n_tokens, n_patch, n_special)
+        if self.sparse_heads:
+            ops.launch_block_select_pooled(pooled_q, pooled_k, buf["sparse_ids"],
+                                           mode=self.mode, topk=buf["topk"], tau=self.tau,
+                                           scale=pooled_q.shape[-1] ** -0.5,
+                                           indices=buf["indices"], counts=buf["counts"])
+        self.last_masks = (buf["indices"], buf["counts"])
+        return buf
+
+    def forward_projected(self, qkv, out=None):
+        """The layer on the outputs of ``vggt_sparse.project_qkv`` (q, split
+        K/V and block means): selection from the means, then attention."""
+        n, npatch, nspecial = qkv.q.shape[1], qkv.patch_k.shape[1], qkv.special_k.shape[1]
+        self.estimate_pooled(qkv.pooled_q, qkv.pooled_k, n, npatch, nspecial)
+        return self.attend(qkv.q, qkv.patch_k, qkv.patch_v, qkv.special_k, qkv.special_v,
+                           out=out)
+
     def attend(self, q, kp, vp, ks, vs, out=None):
         """Block-sparse attention with the masks of the last ``estimate``."""
         h, n, d = q.shape

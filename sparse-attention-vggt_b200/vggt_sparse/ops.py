@@ -149,6 +149,31 @@ def launch_block_mask_estimate(q, k_patch, head_ids, *, query_block, key_block, 
     return indices, counts, scores
 
 
+def launch_block_select_pooled(pooled_q, pooled_k, head_ids, *, mode, topk=None, tau=None,
+                               scale, indices, counts, scores=None, status=None):
+    """Enqueue scores + selection from block means of every head (pooled_q
+    [H, QB, d], pooled_k [H, NB, d] fp32); slot s uses head head_ids[s]."""
+    _require_cuda(pooled_q, pooled_k, head_ids, indices, counts, scores, status)
+    _require_contig(pooled_q=pooled_q, pooled_k=pooled_k, head_ids=head_ids, indices=indices,
+                    counts=counts, scores=scores)
+    if pooled_q.dtype != torch.float32 or pooled_k.dtype != torch.float32:
+        raise ValueError("pooled means must be float32")
+    if pooled_q.dim() != 3 or pooled_k.dim() != 3 or pooled_q.shape[0] != pooled_k.shape[0] or \
+            pooled_q.shape[2] != pooled_k.shape[2]:
+        raise ValueError("pooled_q [H, QB, d] and pooled_k [H, NB, d] expected")
+    h, qbc, d = pooled_q.shape
+    if indices.shape[:2] != (head_ids.numel(), qbc) or counts.shape != (head_ids.numel(), qbc):
+        raise ValueError("indices [slots, QB, max_blocks] and counts [slots, QB] expected")
+    lib = _lib.load()
+    rc = lib.vggt_block_select_pooled(
+        _ptr(pooled_q), _ptr(pooled_k), h, _ptr(head_ids), head_ids.numel(), qbc,
+        pooled_k.shape[1], d, MODES[mode], int(topk or 0), float(tau or 0.0), float(scale),
+        _ptr(indices), indices.shape[-1], _ptr(counts), _ptr(scores), _ptr(status),
+        _stream(pooled_q.device))
+    _lib.check(rc)
+    return indices, counts
+
+
 def launch_block_select(scores, *, mode, topk=None, tau=None, indices, counts):
     """Enqueue selection from fp32 scores [..., n_blocks]."""
     _require_cuda(scores, indices, counts)

@@ -29,7 +29,9 @@ def test_header_declares_the_documented_entry_points():
     assert declared_symbols() == sorted([
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
         "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
-        "vggt_block_select", "vggt_frame_qk_topk", "vggt_history_update", "vggt_sparse_last_error",
+        "vggt_block_select", "vggt_block_select_pooled", "vggt_frame_qk_topk",
+        "vggt_history_update", "vggt_qkv_project_pool", "vggt_qkv_workspace_size",
+        "vggt_sparse_last_error",
         "vggt_sparse_set_wait_limit_ns", "vggt_sparse_set_wait_selftest", "vggt_sparse_version", "vggt_token_sparse_attention"])
 
 
