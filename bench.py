@@ -852,7 +852,8 @@ def run_qkv_bench(args):
     grid = torch.stack((yy.flatten() + 1, xx.flatten() + 1), -1)
     pos = torch.cat((torch.zeros(spf, 2, dtype=torch.long, device=dev), grid)).repeat(
         cfg.frames, 1)
-    cos, sin = vggt_sparse.rope_tables(int(pos.max()) + 1, 100.0, dev)
+    pos_count = gh + 1
+    cos, sin = vggt_sparse.rope_tables(pos_count, 100.0, dev)
     fr = torch.arange(cfg.frames, device=dev)[:, None] * tpf
     patches = (fr + spf + torch.arange(tpf - spf, device=dev)[None]).reshape(-1)
     specials = (fr + torch.arange(spf, device=dev)[None]).reshape(-1)
@@ -884,12 +885,12 @@ def run_qkv_bench(args):
 
     def fusedf():
         out = vggt_sparse.project_qkv(x, w, b, heads=heads, tokens_per_frame=tpf, q_norm=qn,
-                                      k_norm=kn, pos=pos)
+                                      k_norm=kn, pos=pos, pos_count=pos_count)
         return fused.forward_projected(out)
 
     def proj_only():
         return vggt_sparse.project_qkv(x, w, b, heads=heads, tokens_per_frame=tpf, q_norm=qn,
-                                       k_norm=kn, pos=pos)
+                                       k_norm=kn, pos=pos, pos_count=pos_count)
 
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
 

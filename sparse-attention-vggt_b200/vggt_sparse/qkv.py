@@ -70,12 +70,16 @@ class QkvOut:
 
 
 def project_qkv(x, w_qkv, b_qkv=None, *, heads, tokens_per_frame, special_per_frame=5,
-                q_norm=None, k_norm=None, pos=None, rope_base=100.0, pool=True, status=None):
+                q_norm=None, k_norm=None, pos=None, rope_base=100.0, pool=True, status=None,
+                pos_count=None):
     """x [N, C] (or [1, N, C]) bf16/fp16 CUDA, C = 64 * heads; w_qkv [3C, C] and
     b_qkv [3C] (the nn.Linear's weight and bias, converted to x's dtype as
     autocast does); q_norm / k_norm: LayerNorm(64) modules or (weight, bias[,
     eps]) pairs, or None; pos: [N, 2] int (y, x) token positions for RoPE-2D
-    (as VGGT's aggregator builds them), or None.  Returns a QkvOut."""
+    (as VGGT's aggregator builds them), or None; ``pos_count`` (largest
+    position + 1) saves the host read of pos.max() that computing it costs
+    (the kernel clamps positions to [0, pos_count - 1]).
+    Returns a QkvOut."""
     if x.dim() == 3:
         if x.shape[0] != 1:
             raise ValueError("batch one only")
@@ -106,12 +110,14 @@ def project_qkv(x, w_qkv, b_qkv=None, *, heads, tokens_per_frame, special_per_fr
         raise ValueError("q_norm and k_norm must share eps")
     eps = qeps if qeps is not None else (keps if keps is not None else 1e-5)
     cos = sin = None
-    pos_count = 0
-    if pos is not None:
+    if pos is None:
+        pos_count = 0
+    else:
         pos = pos.reshape(-1, 2).to(device=dev, dtype=torch.int32).contiguous()
         if pos.shape[0] != n:
             raise ValueError("pos must be [N, 2]")
-        pos_count = int(pos.max()) + 1 if n else 1
+        if pos_count is None:
+            pos_count = int(pos.max()) + 1 if n else 1  # one host read
         cos, sin = _cached_tables(pos_count, rope_base, dev)
     empty = lambda rows: torch.empty((heads, rows, 64), device=dev, dtype=x.dtype)
     q, kp, vp, ks, vs = empty(n), empty(npatch), empty(npatch), empty(nspecial), empty(nspecial)
