@@ -14,14 +14,17 @@
 // One work tile = 128 token rows x one head: a tcgen05 GEMM of M=128, N=192
 // (the head's 64 q, 64 k and 64 v rows of W, three TMA boxes per K step),
 // K = model dim in steps of 64 through a 3-stage TMA ring, fp32 accumulator
-// in TMEM.  CTAs are persistent (one per SM) with two TMEM accumulators, so
-// the epilogue of one tile (warps 2-5, one token row per thread) overlaps the
-// MMAs of the next.  A thread holds a whole head row, so LayerNorm and RoPE
-// need no cross-thread traffic; block sums go through a shared-memory
-// transpose in a fixed order (deterministic).  Query blocks never straddle
-// tiles (128 = 2 x 64 rows); patch-key blocks can, so each tile writes its
-// partial sums of the (at most three) patch blocks it touches and a second,
-// small kernel folds a block's partials in tile order.
+// in TMEM.  CTAs are persistent (one per SM) with two TMEM accumulators and
+// two epilogue warpgroups (warps 4-7 and 8-11, one token row per thread)
+// that take alternate tiles, so two tiles' epilogues run at once (two warps
+// per SM sub-partition to hide each other's latencies) while the MMAs of the
+// next tile proceed.  setmaxnreg moves registers from the producer / MMA
+// warpgroup to the epilogue warpgroups.  A thread holds a whole head row, so
+// LayerNorm and RoPE need no cross-thread traffic; block sums go through a
+// shared-memory transpose in a fixed order (deterministic).  Query blocks
+// never straddle tiles (128 = 2 x 64 rows); patch-key blocks can, so each
+// tile writes its partial sums of the (at most three) patch blocks it
+// touches and a second, small kernel folds a block's partials in tile order.
 //
 // Every wait is bounded (1 s); on expiry the CTA raises an abort flag, sets
 // VGGT_STATUS_TIMEOUT, drains its copies and MMAs, frees TMEM and exits.
@@ -42,7 +45,16 @@ constexpr int HD = 64;      // head dim
 constexpr int BK = 64;      // K per stage
 constexpr int NO = 3 * HD;  // MMA N: q | k | v of one head
 constexpr int NST = 3;
-constexpr int THREADS = 192;
+// warpgroup 0: TMA producer (warp 0), MMA issuer (warp 1), two idle warps;
+// warpgroups 1 and 2: the epilogue, on alternating tiles (accumulator i % 2)
+constexpr int THREADS = 384;
+// register split (setmaxnreg): the launch gives every thread LAUNCH_REGS;
+// warpgroup 0 gives back down to CTRL_REGS and the two epilogue warpgroups
+// take the difference: 128 * CTRL_REGS + 256 * EPI_REGS = 384 * LAUNCH_REGS
+constexpr int LAUNCH_REGS = 168;
+constexpr int CTRL_REGS = 56;
+constexpr int EPI_REGS = 224;
+static_assert(128 * CTRL_REGS + 256 * EPI_REGS == THREADS * LAUNCH_REGS, "register split");
 constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
 constexpr uint32_t B_BYTES = NO * BK * 2;  // 24 KB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -51,9 +63,10 @@ constexpr uint64_t LIMIT_NS = 1000000000ull;
 constexpr int TPITCH = HD + 1;             // transpose buffer row pitch (floats)
 
 constexpr uint32_t OFF_STAGE = 0;
-constexpr uint32_t OFF_T = NST * STAGE_BYTES;          // float[BM][TPITCH]
-constexpr uint32_t OFF_ROW = OFF_T + BM * TPITCH * 4;  // int[BM]: patch block of each row
-constexpr uint32_t OFF_BAR = (OFF_ROW + BM * 4 + 7) & ~7u;
+constexpr uint32_t OFF_T = NST * STAGE_BYTES;              // float[2 groups][BM][TPITCH]
+constexpr uint32_t OFF_KINFO = OFF_T + 2 * BM * TPITCH * 4;  // int[2][4 warps][4]: block boundaries
+constexpr uint32_t OFF_LN = OFF_KINFO + 2 * 4 * 4 * 4;     // float[4][64]: q_norm w, b, k_norm w, b
+constexpr uint32_t OFF_BAR = OFF_LN + 4 * HD * 4;
 constexpr int B_FULL = 0;                 // [NST]
 constexpr int B_EMPTY = B_FULL + NST;     // [NST]
 constexpr int B_ACCFULL = B_EMPTY + NST;  // [2]
@@ -61,7 +74,7 @@ constexpr int B_ACCEMPTY = B_ACCFULL + 2; // [2]
 constexpr int B_DRAIN = B_ACCEMPTY + 2;
 constexpr int NBAR = B_DRAIN + 1;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;           // tmem base, abort flag, votes
-constexpr uint32_t OFF_ROPE = (OFF_MISC + 32 + 15) & ~15u;  // float2[pos_count][16] (cos, sin)
+constexpr uint32_t OFF_ROPE = (OFF_MISC + 64 + 15) & ~15u;  // float2[pos_count][16] (cos, sin)
 
 struct Params {
   const void* bias;     // [3C] in x's dtype, or null
@@ -97,6 +110,9 @@ __device__ __forceinline__ float round_t(float v) {
     return __half2float(__float2half_rn(v));
 }
 
+__device__ __forceinline__ float elem_to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float elem_to_float(__half x) { return __half2float(x); }
+
 // patch index of a token, or -1 for a special token
 __device__ __forceinline__ int64_t patch_of(int64_t t, const Params& p) {
   const int64_t f = t / p.tok_per_frame;
@@ -130,8 +146,17 @@ __device__ __forceinline__ void norm_rope(float* v, const float* w, const float*
     const float q =
         ((q8[0] + q8[1]) + (q8[2] + q8[3])) + ((q8[4] + q8[5]) + (q8[6] + q8[7]));
     const float rstd = rsqrtf(q * (1.f / HD) + eps);
+    // w and b are shared-memory copies of the LayerNorm parameters
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
-    for (int i = 0; i < HD; ++i) v[i] = fmaf((v[i] - mean) * rstd, __ldg(w + i), __ldg(b + i));
+    for (int i = 0; i < HD / 4; ++i) {
+      const float4 ww = w4[i], bb = b4[i];
+      v[4 * i + 0] = fmaf((v[4 * i + 0] - mean) * rstd, ww.x, bb.x);
+      v[4 * i + 1] = fmaf((v[4 * i + 1] - mean) * rstd, ww.y, bb.y);
+      v[4 * i + 2] = fmaf((v[4 * i + 2] - mean) * rstd, ww.z, bb.z);
+      v[4 * i + 3] = fmaf((v[4 * i + 3] - mean) * rstd, ww.w, bb.w);
+    }
   }
   if (rope) {
 #pragma unroll
@@ -149,7 +174,19 @@ __device__ __forceinline__ void norm_rope(float* v, const float* w, const float*
   }
 }
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// the 128 threads of epilogue group g (named barrier 1 + g)
+__device__ __forceinline__ void epi_sync(int g) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // 64 consecutive values as 8 16-byte stores
 template <typename T>
@@ -179,7 +216,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* misc = reinterpret_cast<uint32_t*>(sbase + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   float* tbuf = reinterpret_cast<float*>(sbase + OFF_T);
-  int* rowblk = reinterpret_cast<int*>(sbase + OFF_ROW);
   float2* table = reinterpret_cast<float2*>(sbase + OFF_ROPE);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t H = p.heads;
@@ -200,6 +236,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (p.pos != nullptr)
     for (int e = tid; e < p.pos_count * 16; e += THREADS)
       table[e] = make_float2(p.rope_cos[e], p.rope_sin[e]);
+  float* ln = reinterpret_cast<float*>(sbase + OFF_LN);  // q_norm w, b, k_norm w, b
+  if (tid < 4 * HD) {
+    const float* src[4] = {p.qn_w, p.qn_b, p.kn_w, p.kn_b};
+    const float* sp = src[tid / HD];
+    ln[tid] = sp != nullptr ? sp[tid % HD] : 0.f;
+  }
   if (warp == 1) {
     tc::tmem_alloc(base + OFF_MISC, TMEM_COLS);
     tc::tmem_relinquish();
@@ -209,6 +251,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc::tc_fence_after();
   const uint32_t tmem = misc[0];
 
+  // each warpgroup sets its register share at the top of its own branch:
+  // warpgroup 0 gives registers back, the epilogue warpgroups take them
+  if (warp < 4) regs_dec<CTRL_REGS>();
   if (warp == 0) {
     // ================= TMA producer =================
     if (lane == 0) {
@@ -278,27 +323,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::mma_commit(bar(B_DRAIN));
       tc::mbar_wait_drain(bar(B_DRAIN), 0, LIMIT_NS);
     }
-  } else {
-    // ================= epilogue: warps 2-5, one token row per thread =================
+  } else if (warp >= 4) {
+    regs_inc<EPI_REGS>();
+    // ====== epilogue: groups of warps 4-7 and 8-11, one token row per thread ======
+    // group g takes the CTA's tiles i = g, g + 2, ... (accumulator g)
+    const int g = (warp - 4) >> 2;
     const int sub = warp & 3;          // TMEM lane quarter of this warp
     const int row = sub * 32 + lane;   // 0..127
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const bool rope = p.pos != nullptr;
-    volatile int* vote = reinterpret_cast<volatile int*>(misc + 4);  // one flag per warp
-    int64_t i = 0;
-    for (int64_t u = blockIdx.x; u < p.tiles; u += gridDim.x, ++i) {
-      const int b = (int)(i & 1);
+    float* tb = tbuf + g * BM * TPITCH;
+    int* kinfo = reinterpret_cast<int*>(sbase + OFF_KINFO) + g * 16;
+    volatile int* vote = reinterpret_cast<volatile int*>(misc + 8 + 4 * g);  // one flag per warp
+    const T* bias = static_cast<const T*>(p.bias);
+    const bool bias16 = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
+    for (int64_t i = g;; i += 2) {
+      const int64_t u = blockIdx.x + i * gridDim.x;
+      if (u >= p.tiles) break;
+      const int b = g;  // == i & 1
       const int64_t rt = u / H;
       const int h = (int)(u % H);
       const bool got = tc::mbar_wait(bar(B_ACCFULL + b), (uint32_t)((i >> 1) & 1), abort_flag,
                                      LIMIT_NS);
-      // the four warps leave together (the named barriers below are not
-      // bounded, so no warp may stop at one the others never reach)
+      // the group's four warps leave together (the named barriers below are
+      // not bounded, so no warp may stop at one the others never reach)
       const bool warp_ok = __all_sync(0xffffffffu, got);
       if (lane == 0) vote[sub] = warp_ok ? 1 : 0;
-      epi_sync();
+      epi_sync(g);
       const bool all_ok = vote[0] && vote[1] && vote[2] && vote[3];
-      epi_sync();
+      epi_sync(g);
       if (!all_ok) break;
       tc::tc_fence_after();
       const uint32_t acc = tmem + (uint32_t)b * 256u + lane_off;
@@ -312,33 +365,49 @@ __global__ void __launch_bounds__(THREADS, 1)
         py = py < 0 ? 0 : (py >= p.pos_count ? p.pos_count - 1 : py);
         px = px < 0 ? 0 : (px >= p.pos_count ? p.pos_count - 1 : px);
       }
-      const T* bias = static_cast<const T*>(p.bias);
       float v[HD];
-#pragma unroll
+#pragma unroll 1
       for (int part = 0; part < 3; ++part) {
         // accumulator columns [64 part, 64 part + 64): q, k, v of head h
         uint32_t r[64];
         tc::tmem_ld32(acc + (uint32_t)(64 * part), r);
         tc::tmem_ld32(acc + (uint32_t)(64 * part + 32), r + 32);
         tc::tmem_wait_ld();
+        if (part == 2) {
+          // the accumulator is read out: the next tile's MMAs may start
+          tc::tc_fence_before();
+          tc::mbar_arrive(bar(B_ACCEMPTY + b));
+        }
         const int bcol = part * p.heads * HD + h * HD;
 #pragma unroll
         for (int d = 0; d < HD; ++d) v[d] = __uint_as_float(r[d]);
         if (bias != nullptr) {
+          if (bias16) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(bias + bcol);
 #pragma unroll
-          for (int d = 0; d < HD; d += 2) {
-            const float2 bb = ElemOps<T>::to_float2(
-                *reinterpret_cast<const uint32_t*>(bias + bcol + d));
-            v[d] += bb.x;
-            v[d + 1] += bb.y;
+            for (int q = 0; q < HD / 8; ++q) {
+              const uint4 w4 = __ldg(b4 + q);
+              const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 bb = ElemOps<T>::to_float2(wv[e]);
+                v[8 * q + 2 * e] += bb.x;
+                v[8 * q + 2 * e + 1] += bb.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int d = 0; d < HD; ++d)
+              v[d] += elem_to_float(bias[bcol + d]);
           }
         }
         // the Linear's output is rounded to the activation dtype
 #pragma unroll
         for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
         if (part < 2) {
-          norm_rope(v, part == 0 ? p.qn_w : p.kn_w, part == 0 ? p.qn_b : p.kn_b, p.ln_eps, rope,
-                    py, px, table);
+          const bool has_norm = (part == 0 ? p.qn_w : p.kn_w) != nullptr;
+          norm_rope(v, has_norm ? ln + 2 * part * HD : nullptr, ln + (2 * part + 1) * HD,
+                    p.ln_eps, rope, py, px, table);
 #pragma unroll
           for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
         }
@@ -359,25 +428,28 @@ __global__ void __launch_bounds__(THREADS, 1)
           // query-block means: thread (half, col) sums column col over rows
           // [64 half, 64 half + 64) of the tile (four interleaved partial sums)
 #pragma unroll
-          for (int d = 0; d < HD; ++d) tbuf[row * TPITCH + d] = valid ? v[d] : 0.f;
-          epi_sync();
+          for (int d = 0; d < HD; ++d) tb[row * TPITCH + d] = valid ? v[d] : 0.f;
+          epi_sync(g);
           const int half = row >> 6, col = row & 63;
           const int64_t qb = rt * 2 + half;
           if (qb < p.qb_count) {
             float a[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-            for (int j = 0; j < 64; ++j) a[j & 3] += tbuf[(half * 64 + j) * TPITCH + col];
+            for (int j = 0; j < 64; ++j) a[j & 3] += tb[(half * 64 + j) * TPITCH + col];
             const int64_t nrow = p.n - qb * 64 < 64 ? p.n - qb * 64 : 64;
             p.pooled_q[(h * p.qb_count + qb) * HD + col] =
                 ((a[0] + a[1]) + (a[2] + a[3])) / (float)nrow;
           }
-          epi_sync();
+          epi_sync(g);
         }
         if (part == 1 && p.part_k != nullptr) {
-          // patch-key block partial sums over this tile's patch rows: the tile
-          // touches blocks first .. first + 2 at most (128 patch rows); thread
-          // (half, col) sums column col of its 64 rows into one accumulator per
-          // block, then the halves are added (half 0 + half 1)
+          // patch-key block partial sums over this tile's patch rows.  The tile
+          // touches blocks first .. first + 2 at most (128 patch rows), in
+          // nondecreasing order down the rows; special and invalid rows hold
+          // zeros.  So slot s covers the row range [start_s, start_{s+1}) with
+          // start_s the first row whose block slot is >= s, and thread (half,
+          // col) sums column col of its half's rows range by range; the halves
+          // are then added (half 0 + half 1).
           int first = -1;
           {
             const int64_t t0 = rt * BM;
@@ -387,43 +459,64 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (tf < p.n && tf < t0 + BM) first = (int)(patch_of(tf, p) >> 6);
           }
 #pragma unroll
-          for (int d = 0; d < HD; ++d) tbuf[row * TPITCH + d] = pidx >= 0 ? v[d] : 0.f;
-          rowblk[row] = pidx >= 0 ? (int)(pidx >> 6) - first : -1;  // slot 0..2, -1 none
-          epi_sync();
-          const int half = row >> 6, col = row & 63;
-          float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-          int seen = 0;  // bit s: some row of this half falls in slot s
-#pragma unroll 4
-          for (int j = half * 64; j < half * 64 + 64; ++j) {
-            const int sl = rowblk[j];
-            const float x = tbuf[j * TPITCH + col];
-            a0 += sl == 0 ? x : 0.f;
-            a1 += sl == 1 ? x : 0.f;
-            a2 += sl == 2 ? x : 0.f;
-            seen |= sl >= 0 ? 1 << sl : 0;
+          for (int d = 0; d < HD; ++d) tb[row * TPITCH + d] = pidx >= 0 ? v[d] : 0.f;
+          const int sl = pidx >= 0 ? (int)(pidx >> 6) - first : -1;  // slot 0..2, -1 none
+          {
+            // per warp: the first row with slot >= 1 and >= 2, and which
+            // slots occur
+            const unsigned ge1 = __ballot_sync(0xffffffffu, sl >= 1);
+            const unsigned ge2 = __ballot_sync(0xffffffffu, sl >= 2);
+            const unsigned s0 = __ballot_sync(0xffffffffu, sl == 0);
+            const unsigned s1 = __ballot_sync(0xffffffffu, sl == 1);
+            if (lane == 0) {
+              kinfo[sub * 4 + 0] = ge1 ? sub * 32 + __ffs(ge1) - 1 : BM;
+              kinfo[sub * 4 + 1] = ge2 ? sub * 32 + __ffs(ge2) - 1 : BM;
+              kinfo[sub * 4 + 2] = (s0 ? 1 : 0) | (s1 ? 2 : 0) | (ge2 ? 4 : 0);
+            }
           }
-          float* kx = tbuf;  // reuse: [3][64] partials of half 1, then the seen flags
-          epi_sync();
+          epi_sync(g);
+          int start1 = BM, start2 = BM, seen = 0;
+#pragma unroll
+          for (int w2 = 0; w2 < 4; ++w2) {
+            start1 = min(start1, kinfo[w2 * 4 + 0]);
+            start2 = min(start2, kinfo[w2 * 4 + 1]);
+            seen |= kinfo[w2 * 4 + 2];
+          }
+          const int half = row >> 6, col = row & 63;
+          const int lo = half * 64, hi = lo + 64;
+          auto range_sum = [&](int j0, int j1) {
+            j0 = j0 < lo ? lo : (j0 > hi ? hi : j0);
+            j1 = j1 < lo ? lo : (j1 > hi ? hi : j1);
+            float x0 = 0.f, x1 = 0.f;
+            int j = j0;
+            for (; j + 1 < j1; j += 2) {
+              x0 += tb[j * TPITCH + col];
+              x1 += tb[(j + 1) * TPITCH + col];
+            }
+            if (j < j1) x0 += tb[j * TPITCH + col];
+            return x0 + x1;
+          };
+          const float a0 = range_sum(0, start1);
+          const float a1 = range_sum(start1, start2);
+          const float a2 = range_sum(start2, BM);
+          float* kx = tb;  // reuse: [3][64] partials of half 1
+          epi_sync(g);
           if (half == 1) {
             kx[col] = a0;
             kx[64 + col] = a1;
             kx[128 + col] = a2;
-            if (col == 0) rowblk[0] = seen;
           }
-          epi_sync();
+          epi_sync(g);
           if (half == 0) {
             const int64_t pbase = (rt * H + h) * 3;
-            const int both = seen | rowblk[0];
             p.part_k[(pbase + 0) * HD + col] = a0 + kx[col];
             p.part_k[(pbase + 1) * HD + col] = a1 + kx[64 + col];
             p.part_k[(pbase + 2) * HD + col] = a2 + kx[128 + col];
-            if (col < 3) p.part_blk[pbase + col] = (both >> col) & 1 ? first + col : -1;
+            if (col < 3) p.part_blk[pbase + col] = (seen >> col) & 1 ? first + col : -1;
           }
-          epi_sync();
+          epi_sync(g);
         }
       }
-      tc::tc_fence_before();
-      tc::mbar_arrive(bar(B_ACCEMPTY + b));
     }
   }
 
@@ -532,17 +625,22 @@ cudaError_t launch_qkv_pool(const QkvPoolArgs& a, cudaStream_t stream) {
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   const int64_t grid = p.tiles < sms ? p.tiles : sms;
-  if (a.dtype == VGGT_DTYPE_BF16) {
-    auto k = qkv_pool_kernel<__nv_bfloat16>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  // The register split assumes LAUNCH_REGS per thread at launch; with any
+  // other count the epilogue's setmaxnreg.inc could never be satisfied, so
+  // such a build does not launch at all.
+  auto launch = [&](auto k) -> cudaError_t {
+    cudaFuncAttributes fa;
+    cudaError_t r = cudaFuncGetAttributes(&fa, k);
+    if (r != cudaSuccess) return r;
+    if (fa.numRegs != LAUNCH_REGS) return cudaErrorInvalidConfiguration;
+    r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (r != cudaSuccess) return r;
     k<<<(unsigned)grid, THREADS, smem, stream>>>(mx, mw, p);
-  } else {
-    auto k = qkv_pool_kernel<__half>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k<<<(unsigned)grid, THREADS, smem, stream>>>(mx, mw, p);
-  }
+    return cudaSuccess;
+  };
+  e = a.dtype == VGGT_DTYPE_BF16 ? launch(qkv_pool_kernel<__nv_bfloat16>)
+                                 : launch(qkv_pool_kernel<__half>);
+  if (e != cudaSuccess) return e;
   e = cudaGetLastError();
   if (e != cudaSuccess || a.pooled_k == nullptr) return e;
   const int64_t nb = (p.n_patch + 63) / 64;
