@@ -65,7 +65,8 @@ constexpr int TPITCH = HD + 1;             // transpose buffer row pitch (floats
 constexpr uint32_t OFF_STAGE = 0;
 constexpr uint32_t OFF_T = NST * STAGE_BYTES;              // float[2 groups][BM][TPITCH]
 constexpr uint32_t OFF_KINFO = OFF_T + 2 * BM * TPITCH * 4;  // int[2][4 warps][4]: block boundaries
-constexpr uint32_t OFF_LN = OFF_KINFO + 2 * 4 * 4 * 4;     // float[4][64]: q_norm w, b, k_norm w, b
+constexpr uint32_t OFF_KX = OFF_KINFO + 2 * 4 * 4 * 4;     // float[2][3][64]: half-1 key partials
+constexpr uint32_t OFF_LN = OFF_KX + 2 * 3 * HD * 4;       // float[4][64]: q_norm w, b, k_norm w, b
 constexpr uint32_t OFF_BAR = OFF_LN + 4 * HD * 4;
 constexpr int B_FULL = 0;                 // [NST]
 constexpr int B_EMPTY = B_FULL + NST;     // [NST]
@@ -74,7 +75,7 @@ constexpr int B_ACCEMPTY = B_ACCFULL + 2; // [2]
 constexpr int B_DRAIN = B_ACCEMPTY + 2;
 constexpr int NBAR = B_DRAIN + 1;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;           // tmem base, abort flag, votes
-constexpr uint32_t OFF_ROPE = (OFF_MISC + 64 + 15) & ~15u;  // float2[pos_count][16] (cos, sin)
+constexpr uint32_t OFF_ROPE = (OFF_MISC + 128 + 15) & ~15u;  // float2[pos_count][16] (cos, sin)
 
 struct Params {
   const void* bias;     // [3C] in x's dtype, or null
@@ -98,27 +99,37 @@ struct Params {
   int heads, k_steps;   // model dim / 64
   int tok_per_frame, special_per_frame;
   int pos_count;        // rows of the RoPE tables (largest position + 1)
+  int bias_smem;        // 1: the bias is staged in shared memory as fp32 (after the RoPE table)
   float ln_eps;
   int64_t tiles;        // row tiles x heads
 };
 
-template <typename T>
-__device__ __forceinline__ float round_t(float v) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value)
-    return __bfloat162float(__float2bfloat16_rn(v));
-  else
-    return __half2float(__float2half_rn(v));
-}
-
 __device__ __forceinline__ float elem_to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float elem_to_float(__half x) { return __half2float(x); }
 
-// patch index of a token, or -1 for a special token
-__device__ __forceinline__ int64_t patch_of(int64_t t, const Params& p) {
-  const int64_t f = t / p.tok_per_frame;
-  const int64_t j = t - f * p.tok_per_frame;
-  if (j < p.special_per_frame) return -1;
-  return f * (p.tok_per_frame - p.special_per_frame) + (j - p.special_per_frame);
+// patch index of a token, or -1 for a special token (token counts stay
+// below 2^31, which the host checks, so 32-bit unsigned division suffices)
+__device__ __forceinline__ int patch_of(uint32_t t, const Params& p) {
+  const uint32_t tpf = (uint32_t)p.tok_per_frame, spf = (uint32_t)p.special_per_frame;
+  const uint32_t f = t / tpf;
+  const uint32_t j = t - f * tpf;
+  if (j < spf) return -1;
+  return (int)(f * (tpf - spf) + (j - spf));
+}
+
+// rounds 64 values to the element type: packed words w[32] (what is stored)
+// and, when `back` is set, the rounded values back in v
+template <typename T>
+__device__ __forceinline__ void round_pack(float* v, uint32_t* w, bool back) {
+#pragma unroll
+  for (int i = 0; i < HD / 2; ++i) {
+    w[i] = ElemOps<T>::pack2(v[2 * i], v[2 * i + 1]);
+    if (back) {
+      const float2 f = ElemOps<T>::to_float2(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
 }
 
 // LayerNorm (biased variance, like torch.nn.LayerNorm) and RoPE-2D of one
@@ -140,8 +151,8 @@ __device__ __forceinline__ void norm_rope(float* v, const float* w, const float*
     for (int j = 0; j < 8; ++j) q8[j] = 0.f;
 #pragma unroll
     for (int i = 0; i < HD; ++i) {
-      const float d = v[i] - mean;
-      q8[i & 7] = fmaf(d, d, q8[i & 7]);
+      v[i] -= mean;  // centred once, reused below
+      q8[i & 7] = fmaf(v[i], v[i], q8[i & 7]);
     }
     const float q =
         ((q8[0] + q8[1]) + (q8[2] + q8[3])) + ((q8[4] + q8[5]) + (q8[6] + q8[7]));
@@ -152,10 +163,10 @@ __device__ __forceinline__ void norm_rope(float* v, const float* w, const float*
 #pragma unroll
     for (int i = 0; i < HD / 4; ++i) {
       const float4 ww = w4[i], bb = b4[i];
-      v[4 * i + 0] = fmaf((v[4 * i + 0] - mean) * rstd, ww.x, bb.x);
-      v[4 * i + 1] = fmaf((v[4 * i + 1] - mean) * rstd, ww.y, bb.y);
-      v[4 * i + 2] = fmaf((v[4 * i + 2] - mean) * rstd, ww.z, bb.z);
-      v[4 * i + 3] = fmaf((v[4 * i + 3] - mean) * rstd, ww.w, bb.w);
+      v[4 * i + 0] = fmaf(v[4 * i + 0] * rstd, ww.x, bb.x);
+      v[4 * i + 1] = fmaf(v[4 * i + 1] * rstd, ww.y, bb.y);
+      v[4 * i + 2] = fmaf(v[4 * i + 2] * rstd, ww.z, bb.z);
+      v[4 * i + 3] = fmaf(v[4 * i + 3] * rstd, ww.w, bb.w);
     }
   }
   if (rope) {
@@ -188,19 +199,12 @@ __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
-// 64 consecutive values as 8 16-byte stores
+// 64 consecutive packed values (32 words) as 8 16-byte stores
 template <typename T>
-__device__ __forceinline__ void store_row(T* dst, const float* v) {
+__device__ __forceinline__ void store_row(T* dst, const uint32_t* w) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    uint4 w;
-    w.x = ElemOps<T>::pack2(v[8 * q + 0], v[8 * q + 1]);
-    w.y = ElemOps<T>::pack2(v[8 * q + 2], v[8 * q + 3]);
-    w.z = ElemOps<T>::pack2(v[8 * q + 4], v[8 * q + 5]);
-    w.w = ElemOps<T>::pack2(v[8 * q + 6], v[8 * q + 7]);
-    d[q] = w;
-  }
+  for (int q = 0; q < 8; ++q) d[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
 }
 
 template <typename T>
@@ -236,6 +240,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (p.pos != nullptr)
     for (int e = tid; e < p.pos_count * 16; e += THREADS)
       table[e] = make_float2(p.rope_cos[e], p.rope_sin[e]);
+  if (p.bias_smem) {
+    // the whole bias vector [3C] as fp32, after the RoPE table
+    float* bs = reinterpret_cast<float*>(sbase + OFF_ROPE) + p.pos_count * 32;
+    const T* bsrc = static_cast<const T*>(p.bias);
+    for (int e = tid; e < 3 * p.heads * HD; e += THREADS) bs[e] = elem_to_float(bsrc[e]);
+  }
   float* ln = reinterpret_cast<float*>(sbase + OFF_LN);  // q_norm w, b, k_norm w, b
   if (tid < 4 * HD) {
     const float* src[4] = {p.qn_w, p.qn_b, p.kn_w, p.kn_b};
@@ -334,54 +344,71 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool rope = p.pos != nullptr;
     float* tb = tbuf + g * BM * TPITCH;
     int* kinfo = reinterpret_cast<int*>(sbase + OFF_KINFO) + g * 16;
-    volatile int* vote = reinterpret_cast<volatile int*>(misc + 8 + 4 * g);  // one flag per warp
+    // one flag per warp, double-buffered by tile so that a tile's votes are
+    // read before the group's next-but-one tile overwrites them
+    volatile int* vote0 = reinterpret_cast<volatile int*>(misc + 8 + 8 * g);
+    float* kx = reinterpret_cast<float*>(sbase + OFF_KX) + g * 3 * HD;
     const T* bias = static_cast<const T*>(p.bias);
     const bool bias16 = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
+    const float* bias_s =
+        p.bias_smem ? reinterpret_cast<const float*>(sbase + OFF_ROPE) + p.pos_count * 32 : nullptr;
     for (int64_t i = g;; i += 2) {
       const int64_t u = blockIdx.x + i * gridDim.x;
       if (u >= p.tiles) break;
       const int b = g;  // == i & 1
-      const int64_t rt = u / H;
+      const int rt = (int)(u / H);
       const int h = (int)(u % H);
+      const uint32_t t = (uint32_t)rt * BM + row;
+      const bool valid = t < (uint64_t)p.n;
+      // token positions do not depend on the accumulator: load them first
+      int py = 0, px = 0;
+      if (rope && valid) {
+        py = p.pos[2 * t];
+        px = p.pos[2 * t + 1];
+      }
       const bool got = tc::mbar_wait(bar(B_ACCFULL + b), (uint32_t)((i >> 1) & 1), abort_flag,
                                      LIMIT_NS);
       // the group's four warps leave together (the named barriers below are
       // not bounded, so no warp may stop at one the others never reach)
       const bool warp_ok = __all_sync(0xffffffffu, got);
+      volatile int* vote = vote0 + 4 * (int)((i >> 1) & 1);
       if (lane == 0) vote[sub] = warp_ok ? 1 : 0;
       epi_sync(g);
       const bool all_ok = vote[0] && vote[1] && vote[2] && vote[3];
-      epi_sync(g);
       if (!all_ok) break;
       tc::tc_fence_after();
       const uint32_t acc = tmem + (uint32_t)b * 256u + lane_off;
-      const int64_t t = rt * BM + row;
-      const bool valid = t < p.n;
-      const int64_t pidx = valid ? patch_of(t, p) : -1;
-      int py = 0, px = 0;
-      if (rope && valid) {
-        py = p.pos[2 * t];
-        px = p.pos[2 * t + 1];
-        py = py < 0 ? 0 : (py >= p.pos_count ? p.pos_count - 1 : py);
-        px = px < 0 ? 0 : (px >= p.pos_count ? p.pos_count - 1 : px);
-      }
+      const int pidx = valid ? patch_of(t, p) : -1;
+      py = py < 0 ? 0 : (py >= p.pos_count ? p.pos_count - 1 : py);
+      px = px < 0 ? 0 : (px >= p.pos_count ? p.pos_count - 1 : px);
+      // part j's 64 accumulator columns arrive in r while part j-1 is processed
+      uint32_t r[64];
+      tc::tmem_ld32(acc, r);
+      tc::tmem_ld32(acc + 32u, r + 32);
+      tc::tmem_wait_ld();
       float v[HD];
+      uint32_t w[HD / 2];
 #pragma unroll 1
       for (int part = 0; part < 3; ++part) {
         // accumulator columns [64 part, 64 part + 64): q, k, v of head h
-        uint32_t r[64];
-        tc::tmem_ld32(acc + (uint32_t)(64 * part), r);
-        tc::tmem_ld32(acc + (uint32_t)(64 * part + 32), r + 32);
-        tc::tmem_wait_ld();
-        if (part == 2) {
-          // the accumulator is read out: the next tile's MMAs may start
-          tc::tc_fence_before();
-          tc::mbar_arrive(bar(B_ACCEMPTY + b));
-        }
-        const int bcol = part * p.heads * HD + h * HD;
 #pragma unroll
         for (int d = 0; d < HD; ++d) v[d] = __uint_as_float(r[d]);
-        if (bias != nullptr) {
+        if (part < 2) {
+          tc::tmem_ld32(acc + (uint32_t)(64 * part + 64), r);
+          tc::tmem_ld32(acc + (uint32_t)(64 * part + 96), r + 32);
+        }
+        const int bcol = part * p.heads * HD + h * HD;
+        if (bias_s != nullptr) {
+          const float4* b4 = reinterpret_cast<const float4*>(bias_s + bcol);
+#pragma unroll
+          for (int q = 0; q < HD / 4; ++q) {
+            const float4 bb = b4[q];
+            v[4 * q] += bb.x;
+            v[4 * q + 1] += bb.y;
+            v[4 * q + 2] += bb.z;
+            v[4 * q + 3] += bb.w;
+          }
+        } else if (bias != nullptr) {
           if (bias16) {
             const uint4* b4 = reinterpret_cast<const uint4*>(bias + bcol);
 #pragma unroll
@@ -397,32 +424,37 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           } else {
 #pragma unroll
-            for (int d = 0; d < HD; ++d)
-              v[d] += elem_to_float(bias[bcol + d]);
+            for (int d = 0; d < HD; ++d) v[d] += elem_to_float(bias[bcol + d]);
           }
         }
         // the Linear's output is rounded to the activation dtype
-#pragma unroll
-        for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
+        round_pack<T>(v, w, part < 2);
         if (part < 2) {
           const bool has_norm = (part == 0 ? p.qn_w : p.kn_w) != nullptr;
           norm_rope(v, has_norm ? ln + 2 * part * HD : nullptr, ln + (2 * part + 1) * HD,
                     p.ln_eps, rope, py, px, table);
-#pragma unroll
-          for (int d = 0; d < HD; ++d) v[d] = round_t<T>(v[d]);
+          round_pack<T>(v, w, true);
         }
         if (valid) {
           T* dst;
-          if (part == 0)
-            dst = static_cast<T*>(p.q) + (h * p.n + t) * HD;
-          else if (pidx >= 0)
-            dst = static_cast<T*>(part == 1 ? p.kp : p.vp) + (h * p.n_patch + pidx) * HD;
-          else {
-            const int64_t f = t / p.tok_per_frame;
-            const int64_t sidx = f * p.special_per_frame + (t - f * p.tok_per_frame);
-            dst = static_cast<T*>(part == 1 ? p.ks : p.vs) + (h * p.n_special + sidx) * HD;
+          if (part == 0) {
+            dst = static_cast<T*>(p.q) + ((int64_t)h * p.n + t) * HD;
+          } else if (pidx >= 0) {
+            dst = static_cast<T*>(part == 1 ? p.kp : p.vp) + ((int64_t)h * p.n_patch + pidx) * HD;
+          } else {
+            const uint32_t f = t / (uint32_t)p.tok_per_frame;
+            const uint32_t sidx = f * (uint32_t)p.special_per_frame + (t - f * (uint32_t)p.tok_per_frame);
+            dst = static_cast<T*>(part == 1 ? p.ks : p.vs) + ((int64_t)h * p.n_special + sidx) * HD;
           }
-          store_row<T>(dst, v);
+          store_row<T>(dst, w);
+        }
+        if (part < 2) {
+          tc::tmem_wait_ld();  // part + 1 is in r
+          if (part == 1) {
+            // the accumulator is read out: the next tile's MMAs may start
+            tc::tc_fence_before();
+            tc::mbar_arrive(bar(B_ACCEMPTY + b));
+          }
         }
         if (part == 0 && p.pooled_q != nullptr) {
           // query-block means: thread (half, col) sums column col over rows
@@ -452,11 +484,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           // are then added (half 0 + half 1).
           int first = -1;
           {
-            const int64_t t0 = rt * BM;
-            const int64_t f = t0 / p.tok_per_frame, j = t0 - f * p.tok_per_frame;
-            const int64_t tf = j < p.special_per_frame ? f * p.tok_per_frame + p.special_per_frame
-                                                       : t0;
-            if (tf < p.n && tf < t0 + BM) first = (int)(patch_of(tf, p) >> 6);
+            const uint32_t t0 = (uint32_t)rt * BM, tpf = (uint32_t)p.tok_per_frame;
+            const uint32_t f = t0 / tpf, j = t0 - f * tpf;
+            const uint32_t tf = j < (uint32_t)p.special_per_frame
+                                    ? f * tpf + (uint32_t)p.special_per_frame
+                                    : t0;
+            if (tf < (uint64_t)p.n && tf < t0 + BM) first = patch_of(tf, p) >> 6;
           }
 #pragma unroll
           for (int d = 0; d < HD; ++d) tb[row * TPITCH + d] = pidx >= 0 ? v[d] : 0.f;
@@ -499,8 +532,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float a0 = range_sum(0, start1);
           const float a1 = range_sum(start1, start2);
           const float a2 = range_sum(start2, BM);
-          float* kx = tb;  // reuse: [3][64] partials of half 1
-          epi_sync(g);
           if (half == 1) {
             kx[col] = a0;
             kx[64 + col] = a1;
@@ -514,7 +545,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             p.part_k[(pbase + 2) * HD + col] = a2 + kx[128 + col];
             if (col < 3) p.part_blk[pbase + col] = (seen >> col) & 1 ? first + col : -1;
           }
-          epi_sync(g);
+          // no barrier here: tb is next written after the next tile's vote
+          // barrier, and kx after two more of this group's barriers
         }
       }
     }
@@ -562,6 +594,10 @@ __global__ void __launch_bounds__(256)
 
 static size_t smem_bytes(int pos_count) {
   return 1024 + OFF_ROPE + (size_t)pos_count * 16 * sizeof(float2);
+}
+// with the bias staged in shared memory (fp32, 3C values)
+static size_t smem_bytes_bias(int pos_count, int heads) {
+  return smem_bytes(pos_count) + (size_t)3 * heads * HD * 4;
 }
 
 }  // namespace qkvp
@@ -619,7 +655,8 @@ cudaError_t launch_qkv_pool(const QkvPoolArgs& a, cudaStream_t stream) {
                    ? reinterpret_cast<int32_t*>(
                          ws + (((size_t)rtiles * a.heads * 3 * HD * 4 + 255) & ~(size_t)255))
                    : nullptr;
-  const size_t smem = smem_bytes(p.pos_count);
+  p.bias_smem = a.bias != nullptr && smem_bytes_bias(p.pos_count, a.heads) <= 227u * 1024u;
+  const size_t smem = p.bias_smem ? smem_bytes_bias(p.pos_count, a.heads) : smem_bytes(p.pos_count);
   int sms = 0, dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
