@@ -172,20 +172,33 @@ class FrameShardedLayer:
     ``__call__(q_local, kp_local, vp_local, ks_local, vs_local, out=None)``
     takes this rank's query rows ``rows(n_tokens)`` of q and the patch /
     special K/V of its frames ``frame_range`` (every rank the same number of
-    frames), and returns this rank's output rows.  K and V are all-gathered over NCCL into
-    head-major buffers, one head group at a time in ``groups`` order; group
-    g+1's transfer runs on NCCL's stream while group g's estimator and
-    attention run.  The default order puts the dense-profiled heads first:
-    they need no estimator, so the sparse heads' transfer hides behind them.
+    frames), and returns this rank's output rows.  K and V are all-gathered
+    over NCCL into head-major buffers (one all-gather per head and tensor,
+    coalesced into one launch on NCCL's stream).
+
+    ``schedule="kfirst"`` (default): one layer over all heads; the patch keys
+    move first, and V and the specials follow on NCCL's stream while the
+    estimator runs on the full keys, so only the key transfer is exposed.
+    ``schedule="groups"``: one layer per head group in ``groups`` order
+    (default: the dense-profiled heads, then the rest); group g+1's transfer
+    runs while group g computes, at the price of one attention launch per
+    group.
     """
 
-    def __init__(self, heads, world, rank, frames, *, dense_heads=(), groups=None, group=None,
-                 **layer_kwargs):
+    def __init__(self, heads, world, rank, frames, *, dense_heads=(), schedule="kfirst",
+                 groups=None, group=None, **layer_kwargs):
         if frames % world:
             raise ValueError("frames (%d) must divide evenly over %d ranks" % (frames, world))
+        if schedule not in ("kfirst", "groups"):
+            raise ValueError("schedule must be 'kfirst' or 'groups'")
         self.world, self.rank, self.frames, self.group = world, rank, frames, group
+        self.schedule = schedule
         dense = sorted(set(int(h) for h in dense_heads))
-        if groups is None:
+        if schedule == "kfirst":
+            if groups is not None:
+                raise ValueError("groups apply to schedule='groups' only")
+            groups = [list(range(heads))]
+        elif groups is None:
             rest = [h for h in range(heads) if h not in set(dense)]
             groups = [g for g in (dense, rest) if g]
         flat = sorted(h for g in groups for h in g)
@@ -222,22 +235,41 @@ class FrameShardedLayer:
             self._full[key] = buf
         return buf
 
+    def gather(self, kp_local, vp_local, ks_local, vs_local):
+        """Enqueues this layer's K/V all-gathers into its full buffers in the
+        order the schedule consumes them; returns one handle per step
+        (``wait()`` orders the current stream after that transfer)."""
+        kp, vp, ks, vs = self._buffers(kp_local, ks_local)
+        if self.schedule == "kfirst":
+            heads = self.groups[0]
+            return [gather_heads_async(((kp_local, kp),), heads, self.world, self.group),
+                    gather_heads_async(((vp_local, vp), (ks_local, ks), (vs_local, vs)), heads,
+                                       self.world, self.group)]
+        pairs = ((kp_local, kp), (vp_local, vp), (ks_local, ks), (vs_local, vs))
+        return [gather_heads_async(pairs, g, self.world, self.group) for g in self.groups]
+
     def __call__(self, q_local, kp_local, vp_local, ks_local, vs_local, out=None):
         # every rank holds the same number of frames
         n_tokens = self.world * (kp_local.shape[1] + ks_local.shape[1])
         kp, vp, ks, vs = self._buffers(kp_local, ks_local)
-        pairs = ((kp_local, kp), (vp_local, vp), (ks_local, ks), (vs_local, vs))
         for layer in self.layers:
             if layer.mode == "topk" and layer.topk is None:
                 # the budget follows the FULL layer, as the reference computes it
                 from .layer import topk_budget
                 nb = math.ceil(kp.shape[1] / layer.block)
                 layer.topk = topk_budget(layer.retention, n_tokens, ks.shape[1], nb, layer.block)
-        # every group's transfer is enqueued up front; each group's compute
-        # waits only for its own heads
-        pending = [gather_heads_async(pairs, g, self.world, self.group) for g in self.groups]
+        # every transfer is enqueued up front; each compute step waits only
+        # for what it reads
+        pending = self.gather(kp_local, vp_local, ks_local, vs_local)
         if out is None:
             out = torch.empty_like(q_local)
+        if self.schedule == "kfirst":
+            layer = self.layers[0]
+            pending[0].wait()
+            layer.estimate(q_local, kp, ks.shape[1])
+            pending[1].wait()
+            layer.attend(q_local, kp, vp, ks, vs, out=out)
+            return out
         for layer, work in zip(self.layers, pending):
             work.wait()
             layer(q_local, kp, vp, ks, vs, out=out)

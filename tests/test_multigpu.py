@@ -54,7 +54,7 @@ def _worker(rank, world, port, result_q):
         kp_full = vd.allgather_frames(x.kp[:, f0 * ppf:f1 * ppf].contiguous(), world)
         ok["allgather"] = bool(torch.equal(kp_full, x.kp))
         # sequence-parallel layer: this rank's query rows and its own frames'
-        # K/V in, NCCL all-gathers of K/V (by head group) inside the call
+        # K/V in, NCCL all-gathers of K/V inside the call (keys first)
         fs = vd.FrameShardedLayer(16, world, rank, 4, **kw)
         s0, s1 = fs.rows(x.shape.n_tokens)
         spf = 5
@@ -62,6 +62,10 @@ def _worker(rank, world, port, result_q):
                  [t[:, f0 * spf:f1 * spf].contiguous() for t in (x.ks, x.vs)]
         fs_out = fs(x.q[:, s0:s1].contiguous(), *shards)
         ok["frames"] = bool(torch.equal(fs_out, full[:, s0:s1]))
+        # the other schedule: one layer per head group (dense heads first)
+        fsg = vd.FrameShardedLayer(16, world, rank, 4, schedule="groups", **kw)
+        out_g = fsg(x.q[:, s0:s1].contiguous(), *shards)
+        ok["frames_groups"] = bool(torch.equal(out_g, full[:, s0:s1]))
         torch.cuda.synchronize()
         result_q.put((rank, ok))
     except Exception as e:  # report instead of leaving the peer waiting
@@ -84,5 +88,6 @@ def test_two_gpu_shards_match_single_gpu_layer():
     for p in procs:
         p.join(timeout=60)
     for rank, ok in results.items():
-        assert ok == {"qblocks": True, "heads": True, "allgather": True, "frames": True}, \
+        assert ok == {"qblocks": True, "heads": True, "allgather": True, "frames": True,
+                      "frames_groups": True}, \
             (rank, ok)
