@@ -228,6 +228,33 @@ __device__ int select_row_warp(float* __restrict__ srow, int nb, int mode, int64
         }
         ncand = written <= kCandCap ? written : -1;
         __syncwarp();
+        if (ncand >= 0 && ncand <= 32) {
+          // Few candidates left (typically after three passes): settle the
+          // remaining digits at once, one candidate per lane.  The remaining
+          // passes would end on the largest candidate key K with
+          // above + W(candidates with key >= K) >= target; the weight of the
+          // candidates above K then joins `above`.  Same integer weights, so
+          // the same selection.
+          const bool have = lane < ncand;
+          const uint32_t key = have ? keys[hist->cand[lane]] : 0u;
+          const unsigned long long w =
+              !have ? 0ull
+                    : (mass ? det_mass_weight(__uint_as_float(key_to_bits(key)), rowmax) : 1ull);
+          unsigned long long ge = 0ull;
+          for (int j = 0; j < ncand; ++j) {
+            const uint32_t kj = __shfl_sync(full, key, j);
+            const unsigned long long wj = __shfl_sync(full, w, j);
+            if (kj >= key) ge += wj;
+          }
+          const uint32_t kb = __reduce_max_sync(full, (have && above_w + ge >= target) ? key : 0u);
+          unsigned long long gt = (have && key > kb) ? w : 0ull;
+#pragma unroll
+          for (int off = 16; off; off >>= 1) gt += __shfl_xor_sync(full, gt, off);
+          above_w += gt;
+          prefix = kb;
+          prefix_mask = 0xffffffffu;
+          break;
+        }
       }
     }
   }
