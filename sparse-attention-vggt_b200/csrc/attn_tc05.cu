@@ -66,8 +66,8 @@ constexpr int B_QFULL = 0;
 constexpr int B_KVFULL = 1;                 // [NSTAGE]
 constexpr int B_KVEMPTY = B_KVFULL + NSTAGE;  // [NSTAGE]
 constexpr int B_SFULL = B_KVEMPTY + NSTAGE;   // [2]
-constexpr int B_PFULL = B_SFULL + 2;          // [2]
-constexpr int B_PVDONE = B_PFULL + 2;         // one phase per PV MMA
+constexpr int B_PFULL = B_SFULL + 2;          // [2 buffers][2 column halves]
+constexpr int B_PVDONE = B_PFULL + 4;         // one phase per PV MMA
 constexpr int B_OFULL = B_PVDONE + 1;         // the last PV MMA is done
 constexpr int B_DRAIN = B_OFULL + 1;          // MMA completion before TMEM release
 constexpr int B_NEVER = B_DRAIN + 1;          // nothing arrives (wait self-test)
@@ -306,7 +306,8 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar(B_SFULL + b), 1);
-      tc::mbar_init(bar(B_PFULL + b), 128);
+      tc::mbar_init(bar(B_PFULL + 2 * b), 128);
+      tc::mbar_init(bar(B_PFULL + 2 * b + 1), 128);
     }
     tc::mbar_init(bar(B_PVDONE), 1);
     tc::mbar_init(bar(B_OFULL), 1);
@@ -440,16 +441,22 @@ __global__ void __launch_bounds__(THREADS, 2)
       auto issue_pv = [&](int64_t u) -> bool {
         const int bu = (int)(u & 1);
         const int su = (int)(u % NSTAGE);
-        if (!tc::mbar_wait(bar(B_PFULL + bu), (uint32_t)((u >> 1) & 1), abort_flag, p.wait_ns))
-          return false;
-        tc::tc_fence_after();
         // MN group 0 = the V tile, group 1 (LBO bytes further) = the ones tile
         const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES,
                                               OFF_ONES - (OFF_V + su * TILE_BYTES));
+        // P arrives in two column halves (keys 0-31, 32-63); each half's two
+        // K = 16 MMAs go as soon as it is published
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          tc::mma_ts(t_o, t_s_of(bu) + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
-                     (u > 0 || kk > 0) ? 1u : 0u);
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!tc::mbar_wait(bar(B_PFULL + 2 * bu + hh), (uint32_t)((u >> 1) & 1), abort_flag,
+                             p.wait_ns))
+            return false;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 2 * hh; kk < 2 * hh + 2; ++kk)
+            tc::mma_ts(t_o, t_s_of(bu) + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
+                       (u > 0 || kk > 0) ? 1u : 0u);
+        }
         tc::mma_commit(bar(B_PVDONE));
         tc::mma_commit(bar(B_KVEMPTY + su));
         return true;
@@ -536,6 +543,15 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tmem_ld32(t_s_of(b) + lane_off + 32u, s + 32);
       tc::tmem_wait_ld();
       uint32_t pk[32];
+      // P is published in two column halves (keys 0-31, then 32-63), so the
+      // MMA issuer starts the first half's PV MMAs while the second half's
+      // exponentials run
+      auto publish = [&](int hh, const uint32_t* src) {
+        tc::tmem_st16(t_s_of(b) + lane_off + 16u * (uint32_t)hh, src);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        tc::mbar_arrive(bar(B_PFULL + 2 * b + hh));
+      };
       if (active) {  // warp-uniform: a warp's 32 rows belong to one query block
         if (ncols < BN) {
 #pragma unroll
@@ -602,7 +618,9 @@ __global__ void __launch_bounds__(THREADS, 2)
             const float ea = ex2(xa), eb = ex2(xb);
             sum += ea + eb;
             pk[i] = ElemOps<T>::pack2(ea, eb);
+            if (i == 15) publish(0, pk);
           }
+          publish(1, pk + 16);
           if (!(mt & 8) && !dense) {  // patch tiles of indexed slots only
             const int64_t qrow = my_qb * 64 + (row & 63);
             float v = my_qb >= 0 && qrow < p.n_tokens ? (mc + __log2f(sum)) * 0.6931471805599453f : 0.f;
@@ -628,9 +646,12 @@ __global__ void __launch_bounds__(THREADS, 2)
         } else if (ncols < BN) {
           // tail tile: masked columns are -inf, which the MUFU path maps to 0
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
+          for (int i = 0; i < 32; ++i) {
             pk[i] = ElemOps<T>::pack2(ex2(fmaf(__uint_as_float(s[2 * i]), c, -mc)),
                                       ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -mc)));
+            if (i == 15) publish(0, pk);
+          }
+          publish(1, pk + 16);
         } else {
           // full tile: x = s * c - m_ref * c two columns at a time (f32x2
           // FMA); the column pairs selected by kPolyPairs go through the
@@ -643,16 +664,16 @@ __global__ void __launch_bounds__(THREADS, 2)
               pk[i] = exp2_poly_pair<T>(xa, xb);
             else
               pk[i] = exp2_mufu_pair<T>(xa, xb);
+            if (i == 15) publish(0, pk);
           }
+          publish(1, pk + 16);
         }
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;
+        publish(0, pk);
+        publish(1, pk + 16);
       }
-      tc::tmem_st32(t_s_of(b) + lane_off, pk);
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      tc::mbar_arrive(bar(B_PFULL + b));
     }
 
     // ---- epilogue: O / l -> out ----
