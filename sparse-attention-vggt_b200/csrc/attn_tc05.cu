@@ -66,8 +66,15 @@ constexpr int B_QFULL = 0;
 constexpr int B_KVFULL = 1;                 // [NSTAGE]
 constexpr int B_KVEMPTY = B_KVFULL + NSTAGE;  // [NSTAGE]
 constexpr int B_SFULL = B_KVEMPTY + NSTAGE;   // [2]
-constexpr int B_PFULL = B_SFULL + 2;          // [2 buffers][2 column halves]
-constexpr int B_PVDONE = B_PFULL + 4;         // one phase per PV MMA
+// P is published in P_PARTS column parts of 64 / P_PARTS keys each
+#ifndef VGGT_TC_P_PARTS
+#define VGGT_TC_P_PARTS 2
+#endif
+constexpr int P_PARTS = VGGT_TC_P_PARTS;
+static_assert(P_PARTS == 2 || P_PARTS == 4, "P parts: 2 or 4");
+constexpr int PAIRS_PER_PART = 32 / P_PARTS;  // packed P columns per part
+constexpr int B_PFULL = B_SFULL + 2;          // [2 buffers][P_PARTS]
+constexpr int B_PVDONE = B_PFULL + 2 * P_PARTS;  // one phase per PV MMA
 constexpr int B_OFULL = B_PVDONE + 1;         // the last PV MMA is done
 constexpr int B_DRAIN = B_OFULL + 1;          // MMA completion before TMEM release
 constexpr int B_NEVER = B_DRAIN + 1;          // nothing arrives (wait self-test)
@@ -306,8 +313,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(bar(B_SFULL + b), 1);
-      tc::mbar_init(bar(B_PFULL + 2 * b), 128);
-      tc::mbar_init(bar(B_PFULL + 2 * b + 1), 128);
+      for (int hh = 0; hh < P_PARTS; ++hh) tc::mbar_init(bar(B_PFULL + P_PARTS * b + hh), 128);
     }
     tc::mbar_init(bar(B_PVDONE), 1);
     tc::mbar_init(bar(B_OFULL), 1);
@@ -444,16 +450,17 @@ __global__ void __launch_bounds__(THREADS, 2)
         // MN group 0 = the V tile, group 1 (LBO bytes further) = the ones tile
         const uint64_t vdesc = tc::sw128_desc(base + OFF_V + su * TILE_BYTES,
                                               OFF_ONES - (OFF_V + su * TILE_BYTES));
-        // P arrives in two column halves (keys 0-31, 32-63); each half's two
-        // K = 16 MMAs go as soon as it is published
+        // P arrives in P_PARTS column parts; each part's K = 16 MMAs go as
+        // soon as it is published
+        constexpr int MMAS = (BN / 16) / P_PARTS;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          if (!tc::mbar_wait(bar(B_PFULL + 2 * bu + hh), (uint32_t)((u >> 1) & 1), abort_flag,
-                             p.wait_ns))
+        for (int hh = 0; hh < P_PARTS; ++hh) {
+          if (!tc::mbar_wait(bar(B_PFULL + P_PARTS * bu + hh), (uint32_t)((u >> 1) & 1),
+                             abort_flag, p.wait_ns))
             return false;
           tc::tc_fence_after();
 #pragma unroll
-          for (int kk = 2 * hh; kk < 2 * hh + 2; ++kk)
+          for (int kk = MMAS * hh; kk < MMAS * hh + MMAS; ++kk)
             tc::mma_ts(t_o, t_s_of(bu) + (uint32_t)(kk * 8), vdesc + (uint64_t)(kk * 128), id_pv,
                        (u > 0 || kk > 0) ? 1u : 0u);
         }
@@ -543,14 +550,21 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc::tmem_ld32(t_s_of(b) + lane_off + 32u, s + 32);
       tc::tmem_wait_ld();
       uint32_t pk[32];
-      // P is published in two column halves (keys 0-31, then 32-63), so the
-      // MMA issuer starts the first half's PV MMAs while the second half's
-      // exponentials run
+      // P is published in column parts (keys 0-31, then 32-63, with two
+      // parts), so the MMA issuer starts a part's PV MMAs while the next
+      // part's exponentials run.  `done` pairs of pk are complete.
       auto publish = [&](int hh, const uint32_t* src) {
-        tc::tmem_st16(t_s_of(b) + lane_off + 16u * (uint32_t)hh, src);
+        if constexpr (PAIRS_PER_PART == 16)
+          tc::tmem_st16(t_s_of(b) + lane_off + (uint32_t)(PAIRS_PER_PART * hh), src);
+        else
+          tc::tmem_st8(t_s_of(b) + lane_off + (uint32_t)(PAIRS_PER_PART * hh), src);
         tc::tmem_wait_st();
         tc::tc_fence_before();
-        tc::mbar_arrive(bar(B_PFULL + 2 * b + hh));
+        tc::mbar_arrive(bar(B_PFULL + P_PARTS * b + hh));
+      };
+      auto publish_done = [&](int done) {  // called after pair done - 1
+        if (done % PAIRS_PER_PART == 0)
+          publish(done / PAIRS_PER_PART - 1, pk + done - PAIRS_PER_PART);
       };
       if (active) {  // warp-uniform: a warp's 32 rows belong to one query block
         if (ncols < BN) {
@@ -618,9 +632,8 @@ __global__ void __launch_bounds__(THREADS, 2)
             const float ea = ex2(xa), eb = ex2(xb);
             sum += ea + eb;
             pk[i] = ElemOps<T>::pack2(ea, eb);
-            if (i == 15) publish(0, pk);
+            publish_done(i + 1);
           }
-          publish(1, pk + 16);
           if (!(mt & 8) && !dense) {  // patch tiles of indexed slots only
             const int64_t qrow = my_qb * 64 + (row & 63);
             float v = my_qb >= 0 && qrow < p.n_tokens ? (mc + __log2f(sum)) * 0.6931471805599453f : 0.f;
@@ -649,9 +662,8 @@ __global__ void __launch_bounds__(THREADS, 2)
           for (int i = 0; i < 32; ++i) {
             pk[i] = ElemOps<T>::pack2(ex2(fmaf(__uint_as_float(s[2 * i]), c, -mc)),
                                       ex2(fmaf(__uint_as_float(s[2 * i + 1]), c, -mc)));
-            if (i == 15) publish(0, pk);
+            publish_done(i + 1);
           }
-          publish(1, pk + 16);
         } else {
           // full tile: x = s * c - m_ref * c two columns at a time (f32x2
           // FMA); the column pairs selected by kPolyPairs go through the
@@ -664,15 +676,14 @@ __global__ void __launch_bounds__(THREADS, 2)
               pk[i] = exp2_poly_pair<T>(xa, xb);
             else
               pk[i] = exp2_mufu_pair<T>(xa, xb);
-            if (i == 15) publish(0, pk);
+            publish_done(i + 1);
           }
-          publish(1, pk + 16);
         }
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;
-        publish(0, pk);
-        publish(1, pk + 16);
+#pragma unroll
+        for (int hh = 0; hh < P_PARTS; ++hh) publish(hh, pk + PAIRS_PER_PART * hh);
       }
     }
 
