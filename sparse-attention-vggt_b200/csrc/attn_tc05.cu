@@ -18,7 +18,9 @@
 //                       in TMEM for the whole key sweep)
 //    and warps 2-5 (128 threads, one query row each) run the softmax: read
 //    S_t, mask tail columns, exp2(s * scale * log2 e - m_ref) with one FFMA
-//    per element, write P_t (bf16/fp16) back to TMEM.  The per-row reference
+//    per element, write P_t (bf16/fp16) back to TMEM in two column halves,
+//    each with its own full barrier, so the MMA lane issues the first half's
+//    PV MMAs while the second half's exponentials run.  The per-row reference
 //    max m_ref only moves when a tile's max exceeds it by more than 8 in the
 //    exp2 domain; O (in TMEM) and the row sum are rescaled then, so P <= 2^8
 //    and the rescale is rare after the first tiles.
