@@ -137,3 +137,46 @@ def test_layer_from_projection_selects_like_the_estimator(cuda):
     for h in fused.sparse_heads[:3]:
         d = np.abs(g[h, rows] - exp[h, rows])
         assert d.max() <= 2e-2 and d.mean() / np.abs(exp[h, rows]).mean() <= 1e-2
+
+
+@pytest.mark.parametrize("heads,bias,extras", [(48, "aligned", True), (48, "offset", True),
+                                               (4, None, False)])
+def test_qkv_projection_variants_against_oracle(cuda, heads, bias, extras):
+    """Paths the VGGT shape does not take: a model too wide for the bias to
+    be staged in shared memory (48 heads: read from global memory, 16-byte
+    vectors when aligned, element by element when the bias starts 4 bytes
+    off), and a plain projection with no bias, LayerNorm or RoPE."""
+    dim, gh, frames = 64 * heads, 6, 2
+    tpf = 5 + gh * gh
+    n = frames * tpf
+    gen = torch.Generator(device="cpu").manual_seed(11 + heads)
+    x = torch.randn(n, dim, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(3 * dim, dim, generator=gen) * dim ** -0.5).to(torch.bfloat16)
+    b = None
+    if bias is not None:
+        full = (torch.randn(3 * dim + 2, generator=gen) * 0.1).to(torch.bfloat16)
+        b = full[2:] if bias == "offset" else full[:3 * dim]
+    ln = (1 + 0.1 * torch.randn(64, generator=gen), 0.1 * torch.randn(64, generator=gen))
+    yy, xx = torch.meshgrid(torch.arange(gh), torch.arange(gh), indexing="ij")
+    grid = torch.stack((yy.flatten() + 1, xx.flatten() + 1), -1)
+    pos = torch.cat((torch.zeros(5, 2, dtype=torch.long), grid)).repeat(frames, 1).int()
+    bd = None
+    if b is not None:
+        store = full.to(cuda)
+        bd = store[2:] if bias == "offset" else store[:3 * dim]
+        assert (bd.data_ptr() % 16 != 0) == (bias == "offset")
+    lnd = tuple(t.to(cuda) for t in ln) if extras else None
+    out = vggt_sparse.project_qkv(x.to(cuda), w.to(cuda), bd, heads=heads, tokens_per_frame=tpf,
+                                  q_norm=lnd, k_norm=lnd, pos=pos.to(cuda) if extras else None)
+    lnn = tuple(t.numpy() for t in ln) if extras else None
+    want = oracle.project_qkv(x.float().numpy(), w.float().numpy(),
+                              b.float().numpy() if b is not None else None, heads, tpf, 5,
+                              lnn, lnn, 1e-5, pos.numpy() if extras else None)
+    for name, wv in zip(NAMES, want[:5]):
+        check_bf16(getattr(out, name), wv)
+    np.testing.assert_allclose(out.pooled_q.cpu().numpy(),
+                               oracle.block_mean(out.q.float().cpu().numpy(), 64)[0], rtol=1e-5,
+                               atol=1e-6)
+    np.testing.assert_allclose(out.pooled_k.cpu().numpy(),
+                               oracle.block_mean(out.patch_k.float().cpu().numpy(), 64)[0],
+                               rtol=1e-5, atol=1e-6)
