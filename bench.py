@@ -1179,9 +1179,9 @@ def main():
         "frames_per_s": cfg.frames / (ms * 1e-3),
         "estimator_ms": est_local, "attention_ms": att_local,
         "allgather": ({"what": "K/V (patch and special) of the other ranks' frames, one NCCL "
-                                "all-gather per head and tensor coalesced into one launch: the "
-                                "patch keys first (exposed), then V and the specials while the "
-                                "estimator runs on the full keys",
+                                "all-gather per tensor into rank-major staging plus one copy "
+                                "into head-major place: the patch keys first (exposed), then V "
+                                "and the specials while the estimator runs on the full keys",
                        "alone": gather_alone} if frame_sharded else None),
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

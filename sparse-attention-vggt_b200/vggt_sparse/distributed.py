@@ -164,6 +164,40 @@ def gather_heads_async(pairs, heads, world, group=None):
     return _Works()
 
 
+def gather_bulk_async(pairs, h0, h1, world, staging, group=None):
+    """All-gather heads [h0, h1) of every (local, full) pair with one
+    collective per tensor: each rank's local[h0:h1] ([h1 - h0, n_local, d],
+    contiguous in the head-major layout) lands rank-major in the matching
+    ``staging`` buffer ([world, h1 - h0, n_local, d]).  The handle's
+    ``wait()`` makes the current stream wait for the transfer, then copies
+    staging into full[h0:h1] ([h1 - h0, world * n_local, d]), the layer's
+    head-major row order.  One large message per tensor and rank instead of
+    one per head keeps NCCL near its bulk rate as the rank count grows."""
+    import torch.distributed as dist
+    # the output as [world * (h1 - h0), n_local, d]: rank-major, the form
+    # every backend accepts
+    calls = [(stg.view((-1,) + tuple(stg.shape[2:])), local[h0:h1])
+             for (local, _), stg in zip(pairs, staging)]
+    if dist.get_backend(group) == "nccl":
+        with dist._coalescing_manager(group=group, device=calls[0][1].device,
+                                      async_ops=True) as cm:
+            for dst, src in calls:
+                dist.all_gather_into_tensor(dst, src, group=group)
+        works = [cm]
+    else:
+        works = [dist.all_gather_into_tensor(dst, src, group=group, async_op=True)
+                 for dst, src in calls]
+
+    class _Bulk:
+        def wait(self):
+            for w in works:
+                w.wait()
+            for (_, full), stg in zip(pairs, staging):
+                hg, n, d = h1 - h0, stg.shape[2], stg.shape[3]
+                full[h0:h1].view(hg, world, n, d).copy_(stg.permute(1, 0, 2, 3))
+    return _Bulk()
+
+
 class FrameShardedLayer:
     """The layer with its K/V sharded by frames and its query blocks split
     across ranks (sequence parallel: what a QKV projection applied to each
@@ -173,8 +207,12 @@ class FrameShardedLayer:
     takes this rank's query rows ``rows(n_tokens)`` of q and the patch /
     special K/V of its frames ``frame_range`` (every rank the same number of
     frames), and returns this rank's output rows.  K and V are all-gathered
-    over NCCL into head-major buffers (one all-gather per head and tensor,
-    coalesced into one launch on NCCL's stream).
+    over NCCL into head-major buffers: ``gather="bulk"`` (default) moves one
+    all-gather per tensor into rank-major staging and copies it into place;
+    ``gather="heads"`` (and any head group that is not a consecutive range)
+    moves one all-gather per head and tensor straight into place (more,
+    smaller messages: slower as the rank count grows).  Either
+    way the calls of one step are coalesced into one launch on NCCL's stream.
 
     ``schedule="kfirst"`` (default): one layer over all heads; the patch keys
     move first, and V and the specials follow on NCCL's stream while the
@@ -186,11 +224,14 @@ class FrameShardedLayer:
     """
 
     def __init__(self, heads, world, rank, frames, *, dense_heads=(), schedule="kfirst",
-                 groups=None, group=None, **layer_kwargs):
+                 groups=None, group=None, gather="bulk", **layer_kwargs):
         if frames % world:
             raise ValueError("frames (%d) must divide evenly over %d ranks" % (frames, world))
         if schedule not in ("kfirst", "groups"):
             raise ValueError("schedule must be 'kfirst' or 'groups'")
+        if gather not in ("heads", "bulk"):
+            raise ValueError("gather must be 'heads' or 'bulk'")
+        self.gather_mode = gather
         self.world, self.rank, self.frames, self.group = world, rank, frames, group
         self.schedule = schedule
         dense = sorted(set(int(h) for h in dense_heads))
@@ -235,6 +276,28 @@ class FrameShardedLayer:
             self._full[key] = buf
         return buf
 
+    def _staging(self, pairs, heads):
+        """Rank-major receive buffers [world, |heads|, n_local, d], one per
+        tensor of ``pairs``, cached by shape."""
+        # one set per head range and tensor list: transfers of different
+        # groups are in flight at the same time
+        key = ("stg", heads[0], len(heads)) + tuple((l.device, l.shape, l.dtype)
+                                                    for l, _ in pairs)
+        stg = self._full.get(key)
+        if stg is None:
+            stg = [torch.empty((self.world, len(heads)) + tuple(l.shape[1:]), device=l.device,
+                               dtype=l.dtype) for l, _ in pairs]
+            self._full[key] = stg
+        return stg
+
+    def _gather(self, pairs, heads):
+        # bulk transfers need a consecutive head range; other groups move
+        # head by head
+        if self.gather_mode == "bulk" and list(heads) == list(range(heads[0], heads[-1] + 1)):
+            return gather_bulk_async(pairs, heads[0], heads[-1] + 1, self.world,
+                                     self._staging(pairs, heads), self.group)
+        return gather_heads_async(pairs, heads, self.world, self.group)
+
     def gather(self, kp_local, vp_local, ks_local, vs_local):
         """Enqueues this layer's K/V all-gathers into its full buffers in the
         order the schedule consumes them; returns one handle per step
@@ -242,11 +305,10 @@ class FrameShardedLayer:
         kp, vp, ks, vs = self._buffers(kp_local, ks_local)
         if self.schedule == "kfirst":
             heads = self.groups[0]
-            return [gather_heads_async(((kp_local, kp),), heads, self.world, self.group),
-                    gather_heads_async(((vp_local, vp), (ks_local, ks), (vs_local, vs)), heads,
-                                       self.world, self.group)]
+            return [self._gather(((kp_local, kp),), heads),
+                    self._gather(((vp_local, vp), (ks_local, ks), (vs_local, vs)), heads)]
         pairs = ((kp_local, kp), (vp_local, vp), (ks_local, ks), (vs_local, vs))
-        return [gather_heads_async(pairs, g, self.world, self.group) for g in self.groups]
+        return [self._gather(pairs, g) for g in self.groups]
 
     def __call__(self, q_local, kp_local, vp_local, ks_local, vs_local, out=None):
         # every rank holds the same number of frames

@@ -84,6 +84,18 @@ def _work(rank, world, result_q):
     for w in works:
         w.wait()
     gather_ok = gather_ok and all(torch.equal(b, t) for b, t in zip(bufs, (x.kp, x.vp, x.ks, x.vs)))
+    # bulk gathers: one collective per tensor into rank-major staging, then
+    # the copy into head-major place (each head range of two groups)
+    bufs = [torch.full_like(t, float("nan")) for t in (x.kp, x.vp, x.ks, x.vs)]
+    pairs = list(zip(locals_, bufs))
+    works = []
+    for h0, h1 in ((1, 2), (0, 1)):
+        stg = [torch.empty((world, h1 - h0) + tuple(l.shape[1:]), dtype=l.dtype)
+               for l in locals_]
+        works.append(vd.gather_bulk_async(pairs, h0, h1, world, stg))
+    for w in works:
+        w.wait()
+    gather_ok = gather_ok and all(torch.equal(b, t) for b, t in zip(bufs, (x.kp, x.vp, x.ks, x.vs)))
     # query-block shard of the oracle layer
     n = x.shape.n_tokens
     b0, b1 = vd.qblock_range(-(-n // 64), world, rank)

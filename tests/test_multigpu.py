@@ -66,6 +66,16 @@ def _worker(rank, world, port, result_q):
         fsg = vd.FrameShardedLayer(16, world, rank, 4, schedule="groups", **kw)
         out_g = fsg(x.q[:, s0:s1].contiguous(), *shards)
         ok["frames_groups"] = bool(torch.equal(out_g, full[:, s0:s1]))
+        # bulk gathers (one all-gather per tensor, then a copy into place)
+        # with both schedules; the groups need consecutive heads
+        kwc = dict(mode="topk", retention=0.25, dense_heads=(0, 1))
+        refc = vggt_sparse.SparseGlobalLayer(16, **kwc)
+        refc.topk = ref.topk
+        fullc = refc(x.q, x.kp, x.vp, x.ks, x.vs)
+        for sched in ("kfirst", "groups"):
+            fsb = vd.FrameShardedLayer(16, world, rank, 4, schedule=sched, gather="bulk", **kwc)
+            out_b = fsb(x.q[:, s0:s1].contiguous(), *shards)
+            ok["frames_bulk_" + sched] = bool(torch.equal(out_b, fullc[:, s0:s1]))
         torch.cuda.synchronize()
         result_q.put((rank, ok))
     except Exception as e:  # report instead of leaving the peer waiting
@@ -89,5 +99,6 @@ def test_two_gpu_shards_match_single_gpu_layer():
         p.join(timeout=60)
     for rank, ok in results.items():
         assert ok == {"qblocks": True, "heads": True, "allgather": True, "frames": True,
-                      "frames_groups": True}, \
+                      "frames_groups": True, "frames_bulk_kfirst": True,
+                      "frames_bulk_groups": True}, \
             (rank, ok)
