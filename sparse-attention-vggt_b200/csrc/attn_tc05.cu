@@ -49,7 +49,10 @@ namespace tcattn {
 constexpr int BM = 128;         // query rows per CTA
 constexpr int BN = 64;          // keys per tile
 constexpr int HD = 64;          // head dim
-constexpr int NSTAGE = 4;       // K/V ring depth
+#ifndef VGGT_TC_NSTAGE
+#define VGGT_TC_NSTAGE 4
+#endif
+constexpr int NSTAGE = VGGT_TC_NSTAGE;  // K/V ring depth
 constexpr int THREADS = 192;
 constexpr uint32_t TILE_BYTES = BN * HD * 2;  // 8 KB
 constexpr uint32_t TMEM_COLS = 256;  // S0 | S1 | O (64 + 16 row-sum cols) | Q: 2 CTAs/SM
