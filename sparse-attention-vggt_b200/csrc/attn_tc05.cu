@@ -20,7 +20,9 @@
 //    S_t, mask tail columns, exp2(s * scale * log2 e - m_ref) with one FFMA
 //    per element, write P_t (bf16/fp16) back to TMEM in two column halves,
 //    each with its own full barrier, so the MMA lane issues the first half's
-//    PV MMAs while the second half's exponentials run.  The per-row reference
+//    PV MMAs while the second half's exponentials run.  A softmax warp probes
+//    its tile's K/V-full and S-full barriers back to back (both are usually
+//    complete) and only then falls back to the bounded waits.  The per-row reference
 //    max m_ref only moves when a tile's max exceeds it by more than 8 in the
 //    exp2 domain; O (in TMEM) and the row sum are rescaled then, so P <= 2^8
 //    and the rescale is rare after the first tiles.
@@ -53,6 +55,9 @@ constexpr int HD = 64;          // head dim
 #define VGGT_TC_NSTAGE 4
 #endif
 constexpr int NSTAGE = VGGT_TC_NSTAGE;  // K/V ring depth
+#ifndef VGGT_TC_PAIRED_PROBE
+#define VGGT_TC_PAIRED_PROBE 1
+#endif
 constexpr int THREADS = 192;
 constexpr uint32_t TILE_BYTES = BN * HD * 2;  // 8 KB
 constexpr uint32_t TMEM_COLS = 256;  // S0 | S1 | O (64 + 16 row-sum cols) | Q: 2 CTAs/SM
@@ -537,10 +542,22 @@ __global__ void __launch_bounds__(THREADS, 2)
     for (int64_t t = 0; t < n_tiles; ++t) {
       const int stage = (int)(t % NSTAGE);
       const int b = (int)(t & 1);
+#if VGGT_TC_PAIRED_PROBE
+      // both barriers are usually complete by now: probe them back to back so
+      // the two probes' latencies overlap, and fall back to the bounded waits
+      // only for one that is not
+      const bool kv_ready = tc::mbar_try_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1));
+      const bool s_ready = tc::mbar_try_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1));
+      bool got = (kv_ready || tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1),
+                                            abort_flag, p.wait_ns)) &&
+                 (s_ready || tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1),
+                                           abort_flag, p.wait_ns));
+#else
       bool got = tc::mbar_wait(bar(B_KVFULL + stage), (uint32_t)((t / NSTAGE) & 1), abort_flag,
                                p.wait_ns) &&
                  tc::mbar_wait(bar(B_SFULL + b), (uint32_t)((t >> 1) & 1), abort_flag,
                                p.wait_ns);
+#endif
       // keep the warp converged for the .sync.aligned TMEM instructions
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
