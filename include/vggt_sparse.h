@@ -125,8 +125,10 @@ int vggt_block_attention(const void* q, const void* patch_k, const void* patch_v
  * partial results: each work item's key tiles are split over 2-4 CTAs and a
  * second launch merges them (output within rounding of the unsplit run; the
  * environment variable VGGT_ATTN_SPLIT=1..4 fixes the split, for both this
- * call and the size query).  workspace == NULL, or a kernel choice other than
- * tcgen05, runs exactly vggt_block_attention.  A workspace smaller than the
+ * call and the size query).  workspace == NULL, a kernel choice other than
+ * tcgen05, or short selections (max_blocks below 64, where the pairing and
+ * the split cost more than they save; VGGT_ATTN_PAIR_MIN sets the threshold)
+ * run exactly vggt_block_attention.  A workspace smaller than the
  * size query is an argument error.
  */
 int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patch_v,

@@ -65,6 +65,19 @@ int64_t attention_split(int64_t items) {
   return vggt::attn_tc05_split(items, current_device_sms());
 }
 
+// Index-row width (selected blocks per query block) below which a workspace
+// call runs exactly the plain launch: with short selections the pairing's
+// four launches and the key-range split cost more than they save (4 frames
+// at top-k 25 %: 0.231 ms paired and split, 0.136 ms plain; 32 frames: 3.79
+// against 4.08 ms).  VGGT_ATTN_PAIR_MIN overrides the default of 64.
+int64_t pair_min_blocks() {
+  if (const char* env = std::getenv("VGGT_ATTN_PAIR_MIN")) {
+    const long v = std::strtol(env, nullptr, 10);
+    if (v >= 0) return v;
+  }
+  return 64;
+}
+
 }  // namespace
 
 extern "C" {
@@ -169,7 +182,7 @@ int vggt_block_attention_ex(const void* q, const void* patch_k, const void* patc
   if (kernel == VGGT_ATTN_TCGEN05 || (kernel == VGGT_ATTN_AUTO && tc_ok)) {
     const size_t need =
         vggt_block_attention_workspace_size(n_tokens, n_patch, n_slots, block_q, block_k);
-    if (workspace != nullptr && need > 0 && max_blocks > 0) {
+    if (workspace != nullptr && need > 0 && max_blocks > 0 && max_blocks >= pair_min_blocks()) {
       if (workspace_bytes < need)
         return fail("workspace of %zu bytes, %zu needed", workspace_bytes, need);
       if (!aligned16(workspace)) return fail("workspace must be 16-byte aligned");

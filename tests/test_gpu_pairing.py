@@ -16,6 +16,13 @@ from vggt_sparse.synthetic import clustered_layer
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _pair_short_selections(monkeypatch):
+    """These tests run the pairing and the key-range split on small layers,
+    whose short selections would otherwise take the plain launch."""
+    monkeypatch.setenv("VGGT_ATTN_PAIR_MIN", "0")
+
 WINDOW = 128
 
 
@@ -168,3 +175,26 @@ def test_work_order_is_a_longest_first_permutation(cuda):
         items = order[slots == slot]
         buckets = np.array([size(i) for i in items]) * 1023 // nb
         assert np.all(np.diff(buckets) <= 0), slot
+
+
+def test_short_selections_take_the_plain_launch(cuda, monkeypatch):
+    """With the default threshold (64 selected blocks per query block), a
+    4-frame top-k 25 % call with a workspace runs exactly the plain launch:
+    no pairing and no key-range split, so the output equals the plain call's
+    bit for bit (the 4-way split the grid size would pick sums differently)."""
+    monkeypatch.delenv("VGGT_ATTN_PAIR_MIN", raising=False)
+    monkeypatch.delenv("VGGT_ATTN_SPLIT", raising=False)
+    x = clustered_layer(4, centres=64, seed=2, device=cuda)
+    heads = torch.arange(16, device=cuda, dtype=torch.int32)
+    k = vggt_sparse.topk_budget(0.25, x.shape.n_tokens, x.shape.n_special, x.shape.n_blocks, 64)
+    assert k < 64
+    res = vggt_sparse.block_mask_estimate(x.q, x.kp, head_ids=heads, mode="topk", topk=k)
+    outs = []
+    for pair in (True, False):
+        out = torch.empty_like(x.q)
+        vggt_sparse.ops.launch_block_attention(x.q, x.kp, x.vp, x.ks, x.vs, res.indices,
+                                               res.counts, heads, out=out, kernel="tcgen05",
+                                               pair_qblocks=pair)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])

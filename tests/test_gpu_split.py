@@ -15,6 +15,13 @@ from vggt_sparse.synthetic import clustered_layer
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _pair_short_selections(monkeypatch):
+    """These tests run the pairing and the key-range split on small layers,
+    whose short selections would otherwise take the plain launch."""
+    monkeypatch.setenv("VGGT_ATTN_PAIR_MIN", "0")
+
+
 def _run(x, idx, cnt, buf, evidence):
     out = torch.zeros_like(x.q)
     ev = torch.full(idx.shape, -float("inf"), device=x.q.device) if evidence else None
