@@ -169,10 +169,44 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
 }
 
-// two polynomial exponentials, packed into the MMA element type
+#ifndef VGGT_TC_POLY_F32X2
+#define VGGT_TC_POLY_F32X2 1
+#endif
+
+// two polynomial exponentials, packed into the MMA element type.  With
+// VGGT_TC_POLY_F32X2 the pair shares one chain of packed f32x2 instructions
+// (same steps, same cubic, same result bits as exp2_poly on each element):
+// the rounding add and the two subtractions are explicit .rn operations, so
+// nothing contracts them into an FMA and the round-to-integer trick holds.
 template <typename T>
 __device__ __forceinline__ uint32_t exp2_poly_pair(float xa, float xb) {
+#if VGGT_TC_POLY_F32X2
+  xa = fmaxf(xa, -126.f);
+  xb = fmaxf(xb, -126.f);
+  float qa, qb, ta, tb;
+  asm("{\n\t.reg .b64 x, m, t, n, f, q, c3, c2, c1, c0;\n\t"
+      "mov.b64 x, {%4, %5};\n\t"
+      "mov.b64 m, {%6, %6};\n\t"
+      "mov.b64 c3, {%7, %7};\n\t"
+      "mov.b64 c2, {%8, %8};\n\t"
+      "mov.b64 c1, {%9, %9};\n\t"
+      "mov.b64 c0, {%10, %10};\n\t"
+      "add.rn.f32x2 t, x, m;\n\t"
+      "sub.rn.f32x2 n, t, m;\n\t"
+      "sub.rn.f32x2 f, x, n;\n\t"
+      "fma.rn.f32x2 q, f, c3, c2;\n\t"
+      "fma.rn.f32x2 q, q, f, c1;\n\t"
+      "fma.rn.f32x2 q, q, f, c0;\n\t"
+      "mov.b64 {%0, %1}, q;\n\t"
+      "mov.b64 {%2, %3}, t;\n\t}"
+      : "=f"(qa), "=f"(qb), "=f"(ta), "=f"(tb)
+      : "f"(xa), "f"(xb), "f"(12582912.f), "f"(0.05517131f), "f"(0.24261053f),
+        "f"(0.69326099f), "f"(0.99992811f));
+  return ElemOps<T>::pack2(__int_as_float(__float_as_int(qa) + (__float_as_int(ta) << 23)),
+                           __int_as_float(__float_as_int(qb) + (__float_as_int(tb) << 23)));
+#else
   return ElemOps<T>::pack2(exp2_poly(xa), exp2_poly(xb));
+#endif
 }
 
 // two MUFU exponentials, packed into the MMA element type.  With
