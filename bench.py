@@ -36,6 +36,20 @@ METRIC = "ms per sparse global-attn layer & kept-block TFLOPS at 32/100 frames; 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+GATHER_WHAT = {
+    "bulk": "K/V (patch and special) of the other ranks' frames, one NCCL all-gather per tensor "
+            "into rank-major staging plus one copy into head-major place: the patch keys first "
+            "(exposed), then V and the specials while the estimator runs on the full keys",
+    "heads": "K/V (patch and special) of the other ranks' frames, NCCL all-gathers per head "
+             "straight into head-major place: the patch keys first (exposed), then V and the "
+             "specials while the estimator runs on the full keys",
+    "push": "K/V (patch and special) of the other ranks' frames: each rank's kernel stores its "
+            "shards into every rank's head-major buffers over NVLink peer memory (symmetric "
+            "memory, bounded handshake in the same launch): the patch keys first (exposed), "
+            "then V and the specials while the estimator runs on the full keys",
+}
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -49,6 +63,11 @@ def parse_args():
                         "every step; qblocks = query-block shards with the layer's K/V "
                         "replicated on every rank (no collective); heads = each rank holds "
                         "only a cost-balanced set of heads (no collective)")
+    p.add_argument("--gather", choices=("bulk", "heads", "push"), default="bulk",
+                   help="kv-allgather transfer: bulk = one NCCL all-gather per tensor, then a "
+                        "copy into place; heads = NCCL all-gathers per head; push = this "
+                        "library's kernel storing each rank's shards into every rank's "
+                        "buffers over NVLink peer memory")
     p.add_argument("--kernel", default="auto")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -979,6 +998,7 @@ def main():
         # NCCL head group by head group, overlapped with the groups' compute
         from vggt_sparse import distributed as vd
         runner = vd.FrameShardedLayer(heads, world, rank, cfg.frames, dense_heads=dense,
+                                      gather=args.gather,
                                       **layer_kwargs)
         f0, f1 = vd.frame_range(cfg.frames, world, rank)
         ppf, spf = x.shape.patch_h * x.shape.patch_w, x.shape.special_per_frame
@@ -1063,6 +1083,8 @@ def main():
         att_ms = [e[2].elapsed_time(e[3]) for e in ev]
         att_local = sum(att_ms) / len(att_ms)
         est_local = sum(est_ms) / len(est_ms)
+    if frame_sharded:
+        runner.check_status()   # a peer-memory exchange whose wait ran out fails the run
     flops_total = reduce_sum(flops_local, world)
     gather_alone = None
     if frame_sharded:
@@ -1169,7 +1191,9 @@ def main():
         "config": {"workload": workload_desc(cfg, x.shape), "frames": cfg.frames,
                    "tokens": x.shape.n_tokens, "heads": 16, "head_dim": 64,
                    "selection": cfg.mode, "dense_heads": list(cfg.dense_heads),
-                   "parallelism": ("%s-sharded x%d" % (args.shard, world)) if world > 1
+                   "parallelism": ("%s-sharded x%d%s" % (
+                       args.shard, world, (", %s transfer" % args.gather)
+                       if args.shard == "kv-allgather" else "")) if world > 1
                    else "single GPU",
                    "l2": "inputs 270 MB > 126 MB L2; 256 MB flush write between timed steps "
                          "(outside the per-step events)",
@@ -1178,11 +1202,8 @@ def main():
         "kept_block_gflop_per_layer": flops_total / 1e9,
         "frames_per_s": cfg.frames / (ms * 1e-3),
         "estimator_ms": est_local, "attention_ms": att_local,
-        "allgather": ({"what": "K/V (patch and special) of the other ranks' frames, one NCCL "
-                                "all-gather per tensor into rank-major staging plus one copy "
-                                "into head-major place: the patch keys first (exposed), then V "
-                                "and the specials while the estimator runs on the full keys",
-                       "alone": gather_alone} if frame_sharded else None),
+        "allgather": ({"what": GATHER_WHAT[args.gather], "alone": gather_alone}
+                      if frame_sharded else None),
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": att_tflops / peaks["bf16_tflops"],

@@ -343,6 +343,36 @@ int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int m
                       int64_t topk, double tau, int32_t* indices, int64_t max_blocks,
                       int32_t* counts, void* stream);
 
+/*
+ * No reference counterpart (the reference runs on one GPU): the K/V exchange
+ * of the sequence-parallel layer over NVLink peer memory.  Every rank keeps
+ * its full head-major K/V buffers in one allocation of the same size and
+ * layout on every rank, mapped into every other rank's address space
+ * (rank_bases[j] = rank j's allocation as this process addresses it), with
+ * vggt_kv_push_flag_bytes(world) bytes of flag words at flags_offset
+ * (zeroed once before the first exchange).  The launch stores this rank's
+ * shard t ([heads, rows_local[t], dim], contiguous) into rows
+ * [rank * rows_local[t], (rank + 1) * rows_local[t]) of every head of full
+ * tensor t ([heads, world * rows_local[t], dim] at byte dst_offsets[t] of
+ * every allocation), and completes once this rank's full buffers hold every
+ * rank's rows.  Every rank makes the same calls in the same order with the
+ * same epoch (>= 1, raised by one per exchange); handshake = 1 on the first
+ * call of an exchange makes every rank wait until all ranks have started it
+ * (their previous readers of the buffers are done), phase 0/1 tells two
+ * calls of one exchange apart.  Nothing reads another GPU's memory.  Waits
+ * are bounded (vggt_sparse_set_wait_limit_ns, else 10 s); on expiry
+ * VGGT_STATUS_TIMEOUT is ORed into *status and the buffers are invalid.
+ * grid <= 0 picks one CTA per multiprocessor.
+ */
+int vggt_kv_push(const void* const* shards, const int64_t* rows_local,
+                 const int64_t* dst_offsets, int n_tensors, int64_t heads, int dim,
+                 int elem_bytes, void* const* rank_bases, int world, int rank,
+                 int64_t flags_offset, int phase, uint32_t epoch, int handshake, int grid,
+                 int32_t* status, void* stream);
+
+/* Bytes of flag words vggt_kv_push needs for `world` ranks (0 if unsupported). */
+int64_t vggt_kv_push_flag_bytes(int world);
+
 #ifdef __cplusplus
 }
 #endif

@@ -505,6 +505,63 @@ int vggt_block_select_pooled(const float* pooled_q, const float* pooled_k, int64
       static_cast<cudaStream_t>(stream)));
 }
 
+int64_t vggt_kv_push_flag_bytes(int world) {
+  if (world < 1 || world > vggt::kKvPushMaxPeers) return 0;
+  return ((int64_t)(3 * world + 4) * 4 + 255) / 256 * 256;
+}
+
+int vggt_kv_push(const void* const* shards, const int64_t* rows_local,
+                 const int64_t* dst_offsets, int n_tensors, int64_t heads, int dim,
+                 int elem_bytes, void* const* rank_bases, int world, int rank,
+                 int64_t flags_offset, int phase, uint32_t epoch, int handshake, int grid,
+                 int32_t* status, void* stream) {
+  g_err[0] = '\0';
+  if (n_tensors < 1 || n_tensors > vggt::kKvPushMaxTensors)
+    return fail("n_tensors must be in [1, %d]", vggt::kKvPushMaxTensors);
+  if (world < 1 || world > vggt::kKvPushMaxPeers)
+    return fail("world must be in [1, %d]", vggt::kKvPushMaxPeers);
+  if (rank < 0 || rank >= world) return fail("rank %d outside [0, %d)", rank, world);
+  if (phase != 0 && phase != 1) return fail("phase must be 0 or 1");
+  if (heads < 0 || dim < 1 || (elem_bytes != 2 && elem_bytes != 4) ||
+      ((int64_t)dim * elem_bytes) % 16)
+    return fail("rows must be a multiple of 16 bytes (dim %d, %d-byte elements)", dim, elem_bytes);
+  if (epoch == 0) return fail("epoch must be >= 1 (the flag words start at 0)");
+  if (!shards || !rows_local || !dst_offsets || !rank_bases)
+    return fail("shards, rows_local, dst_offsets and rank_bases must be non-NULL");
+  if (flags_offset < 0 || flags_offset % 4) return fail("flags_offset must be a multiple of 4");
+  vggt::KvPushArgs a{};
+  a.n_tensors = n_tensors;
+  a.row_units = (int64_t)dim * elem_bytes / 16;
+  int64_t units = 0;
+  for (int t = 0; t < n_tensors; ++t) {
+    if (rows_local[t] < 1) return fail("rows_local[%d] must be >= 1", t);
+    if (!shards[t] || !aligned16(shards[t])) return fail("shard %d must be 16-byte aligned", t);
+    if (dst_offsets[t] < 0 || dst_offsets[t] % 16)
+      return fail("dst_offsets[%d] must be a non-negative multiple of 16", t);
+    a.src[t] = static_cast<const uint4*>(shards[t]);
+    a.rows_local[t] = rows_local[t];
+    a.dst_off[t] = dst_offsets[t];
+    units += heads * rows_local[t] * a.row_units;
+    a.unit_end[t] = units;
+  }
+  for (int j = 0; j < world; ++j) {
+    if (!rank_bases[j] || !aligned16(rank_bases[j]))
+      return fail("rank_bases[%d] must be a 16-byte aligned device address", j);
+    a.peers[j] = rank_bases[j];
+  }
+  a.world = world;
+  a.rank = rank;
+  a.flags_off = flags_offset;
+  a.phase = phase;
+  a.epoch = epoch;
+  a.handshake = handshake ? 1 : 0;
+  a.status = status;
+  const uint64_t lim = g_wait_ns.load();
+  a.wait_ns = lim ? lim : 10000000000ull;  // ranks may start an exchange seconds apart
+  if (grid <= 0) grid = std::max(1, current_device_sms());
+  return cuda_rc(vggt::launch_kv_push(a, grid, static_cast<cudaStream_t>(stream)));
+}
+
 int vggt_block_select(const float* scores, int64_t rows, int64_t n_blocks, int mode, int64_t topk,
                       double tau, int32_t* indices, int64_t max_blocks, int32_t* counts,
                       void* stream) {

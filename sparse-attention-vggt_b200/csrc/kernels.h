@@ -161,4 +161,26 @@ size_t attn_tc05_split_bytes(int64_t items, int64_t nsplit);
 cudaError_t launch_combine_splits(const AttnArgs& a, int64_t items, int nsplit,
                                   cudaStream_t stream);
 
+// kv_push.cu: stores of this rank's frame shards into every rank's full
+// buffers over peer memory (see the file's header for the flag protocol)
+constexpr int kKvPushMaxPeers = 16;
+constexpr int kKvPushMaxTensors = 4;
+struct KvPushArgs {
+  const uint4* src[kKvPushMaxTensors];    // shard t: [heads, rows_local[t], row_units] uint4
+  int64_t rows_local[kKvPushMaxTensors];
+  int64_t dst_off[kKvPushMaxTensors];     // byte offset of full tensor t in every allocation
+  int64_t unit_end[kKvPushMaxTensors];    // cumulative 16-byte units of the shards
+  int n_tensors;
+  int64_t row_units;                      // 16-byte units per row
+  void* peers[kKvPushMaxPeers];           // every rank's allocation base, rank order
+  int world, rank;
+  int64_t flags_off;                      // byte offset of the flag words
+  int phase;                              // 0 or 1: which done/counter words
+  uint32_t epoch;
+  int handshake;
+  int32_t* status;
+  uint64_t wait_ns;
+};
+cudaError_t launch_kv_push(const KvPushArgs& a, int grid, cudaStream_t stream);
+
 }  // namespace vggt

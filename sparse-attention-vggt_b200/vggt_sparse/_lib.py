@@ -39,6 +39,9 @@ SIGNATURES = {
                                       ctypes.c_double, ctypes.c_float, _P, _P, _P, _I64, _P, _P, _P,
                                       _P]),
     "vggt_block_select": (_I, [_P, _I64, _I64, _I, _I64, ctypes.c_double, _P, _I64, _P, _P]),
+    "vggt_kv_push": (_I, [_P, _P, _P, _I, _I64, _I, _I, _P, _I, _I, _I64, _I, ctypes.c_uint32,
+                          _I, _I, _P, _P]),
+    "vggt_kv_push_flag_bytes": (_I64, [_I]),
     "vggt_qkv_workspace_size": (ctypes.c_size_t, [_I64, _I]),
     "vggt_qkv_project_pool": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _P, _P, _P, _P,
                                    ctypes.c_float, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,

@@ -198,6 +198,107 @@ def gather_bulk_async(pairs, h0, h1, world, staging, group=None):
     return _Bulk()
 
 
+class _EventWait:
+    """A transfer handle: ``wait()`` orders the current stream after ``event``."""
+
+    def __init__(self, event):
+        self.event = event
+
+    def wait(self):
+        torch.cuda.current_stream().wait_event(self.event)
+
+
+class _PushExchange:
+    """The frame-shard exchange over NVLink peer memory (``vggt_kv_push``).
+
+    The full head-major kp, vp, ks, vs ([heads, world * n_local, d] each) and
+    the kernel's flag words sit in one symmetric allocation
+    (``torch.distributed._symmetric_memory``): the same size and layout on
+    every rank, every rank's mapped into every other's address space.  Each
+    exchange runs two launches on a side stream: the patch keys (with the
+    start handshake), then V and the special keys and values.  Every launch
+    stores this rank's shards into all ranks' buffers and returns once this
+    rank's buffers hold every rank's rows."""
+
+    def __init__(self, kp_local, ks_local, world, rank, group):
+        import ctypes
+
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+        h, npl, d = kp_local.shape
+        nsl = ks_local.shape[1]
+        es = kp_local.element_size()
+        dev = kp_local.device
+        rows = (npl, npl, nsl, nsl)
+        sizes = [h * world * n * d * es for n in rows]
+        self.offsets, off = [], 0
+        for b in sizes:
+            self.offsets.append(off)
+            off += (b + 255) // 256 * 256
+        self.lib = _lib.load()
+        flag_bytes = self.lib.vggt_kv_push_flag_bytes(world)
+        if flag_bytes <= 0:
+            raise ValueError("the peer-memory exchange supports at most 16 ranks, not %d" % world)
+        self.flags_off = off
+        buf = symm_mem.empty(off + flag_bytes, dtype=torch.uint8, device=dev)
+        buf[off:].zero_()
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm_mem.rendezvous(buf, grp)
+        # the peers' addresses of this allocation, in rank order
+        delta = buf.data_ptr() - int(self.handle.buffer_ptrs[rank])
+        self.bases = (ctypes.c_void_p * world)(*[int(b) + delta for b in self.handle.buffer_ptrs])
+        self.buf = buf
+        self.full = tuple(buf[o:o + b].view(kp_local.dtype).view(h, world * n, d)
+                          for o, b, n in zip(self.offsets, sizes, rows))
+        self.world, self.rank, self.heads, self.dim = world, rank, h, d
+        self.elem = es
+        self.epoch = 0
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.grid = 0
+        # every rank's flag words are zero before any rank signals
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=grp)
+
+    def _push(self, shards, which, phase, handshake):
+        import ctypes
+
+        from . import _lib
+        n = len(shards)
+        ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in shards])
+        rows = (ctypes.c_int64 * n)(*[t.shape[1] for t in shards])
+        offs = (ctypes.c_int64 * n)(*[self.offsets[w] for w in which])
+        rc = self.lib.vggt_kv_push(ptrs, rows, offs, n, self.heads, self.dim, self.elem,
+                                   self.bases, self.world, self.rank, self.flags_off, phase,
+                                   self.epoch, handshake, self.grid, self.status.data_ptr(),
+                                   self.stream.cuda_stream)
+        _lib.check(rc)
+
+    def exchange(self, kp_local, vp_local, ks_local, vs_local):
+        """Enqueues one exchange; returns the handles of the keys and of the rest."""
+        shards = [t.contiguous() for t in (kp_local, vp_local, ks_local, vs_local)]
+        self.stream.wait_stream(torch.cuda.current_stream())   # shards written, readers done
+        self.epoch = self.epoch % 0x7fffffff + 1
+        with torch.cuda.stream(self.stream):
+            self._push(shards[:1], (0,), 0, 1)
+            ev_k = torch.cuda.Event()
+            ev_k.record(self.stream)
+            self._push(shards[1:], (1, 2, 3), 1, 0)
+            ev_v = torch.cuda.Event()
+            ev_v.record(self.stream)
+        for t in shards:
+            t.record_stream(self.stream)
+        return [_EventWait(ev_k), _EventWait(ev_v)]
+
+    def check_status(self):
+        """Raises if a wait of an exchange ran out (synchronises)."""
+        if int(self.status.item()):
+            raise RuntimeError("a K/V exchange wait ran out (status %d): outputs are invalid"
+                               % int(self.status.item()))
+
+
 class FrameShardedLayer:
     """The layer with its K/V sharded by frames and its query blocks split
     across ranks (sequence parallel: what a QKV projection applied to each
@@ -213,6 +314,10 @@ class FrameShardedLayer:
     moves one all-gather per head and tensor straight into place (more,
     smaller messages: slower as the rank count grows).  Either
     way the calls of one step are coalesced into one launch on NCCL's stream.
+    ``gather="push"`` (``schedule="kfirst"`` only) skips NCCL: the full
+    buffers live in symmetric memory and ``vggt_kv_push`` stores each rank's
+    shards straight into every rank's buffers over NVLink, with a bounded
+    handshake in the same launch (``check_status()`` reports an expired wait).
 
     ``schedule="kfirst"`` (default): one layer over all heads; the patch keys
     move first, and V and the specials follow on NCCL's stream while the
@@ -229,8 +334,10 @@ class FrameShardedLayer:
             raise ValueError("frames (%d) must divide evenly over %d ranks" % (frames, world))
         if schedule not in ("kfirst", "groups"):
             raise ValueError("schedule must be 'kfirst' or 'groups'")
-        if gather not in ("heads", "bulk"):
-            raise ValueError("gather must be 'heads' or 'bulk'")
+        if gather not in ("heads", "bulk", "push"):
+            raise ValueError("gather must be 'heads', 'bulk' or 'push'")
+        if gather == "push" and schedule != "kfirst":
+            raise ValueError("gather='push' runs with schedule='kfirst'")
         self.gather_mode = gather
         self.world, self.rank, self.frames, self.group = world, rank, frames, group
         self.schedule = schedule
@@ -264,7 +371,23 @@ class FrameShardedLayer:
         per = (kp_local.numel() + ks_local.numel()) * kp_local.element_size() * 2
         return per * (self.world - 1)
 
+    def _exchange(self, kp_local, ks_local):
+        key = ("push", kp_local.device, kp_local.shape, ks_local.shape, kp_local.dtype)
+        ex = self._full.get(key)
+        if ex is None:
+            ex = _PushExchange(kp_local, ks_local, self.world, self.rank, self.group)
+            self._full[key] = ex
+        return ex
+
+    def check_status(self):
+        """Raises if a wait of a peer-memory exchange ran out (synchronises)."""
+        for v in self._full.values():
+            if isinstance(v, _PushExchange):
+                v.check_status()
+
     def _buffers(self, kp_local, ks_local):
+        if self.gather_mode == "push":
+            return self._exchange(kp_local, ks_local).full
         key = (kp_local.device, kp_local.shape, ks_local.shape, kp_local.dtype)
         buf = self._full.get(key)
         if buf is None:
@@ -302,6 +425,9 @@ class FrameShardedLayer:
         """Enqueues this layer's K/V all-gathers into its full buffers in the
         order the schedule consumes them; returns one handle per step
         (``wait()`` orders the current stream after that transfer)."""
+        if self.gather_mode == "push":
+            return self._exchange(kp_local, ks_local).exchange(kp_local, vp_local, ks_local,
+                                                               vs_local)
         kp, vp, ks, vs = self._buffers(kp_local, ks_local)
         if self.schedule == "kfirst":
             heads = self.groups[0]

@@ -30,7 +30,8 @@ def test_header_declares_the_documented_entry_points():
         "vggt_block_attention", "vggt_block_attention_ex", "vggt_block_attention_workspace_size",
         "vggt_block_mask_assemble", "vggt_block_mask_estimate", "vggt_block_mask_estimate_noalloc",
         "vggt_block_select", "vggt_block_select_pooled", "vggt_frame_qk_topk",
-        "vggt_history_update", "vggt_qkv_project_pool", "vggt_qkv_workspace_size",
+        "vggt_history_update", "vggt_kv_push", "vggt_kv_push_flag_bytes",
+        "vggt_qkv_project_pool", "vggt_qkv_workspace_size",
         "vggt_sparse_last_error",
         "vggt_sparse_set_wait_limit_ns", "vggt_sparse_set_wait_selftest", "vggt_sparse_version", "vggt_token_sparse_attention"])
 
@@ -173,6 +174,23 @@ def test_token_attention_argument_errors(lib):
         assert call(**bad) < 0
         assert msg in lib.vggt_sparse_last_error().decode()
     assert call(n=0) == 0
+
+
+def test_kv_push_argument_errors(lib):
+    assert lib.vggt_kv_push_flag_bytes(8) == 256 and lib.vggt_kv_push_flag_bytes(17) == 0
+    two = lambda *v: (ctypes.c_void_p * 2)(*v)
+    i64 = lambda *v: (ctypes.c_int64 * len(v))(*v)
+    call = lambda **kw: lib.vggt_kv_push(*dict(dict(
+        shards=two(256, 512), rows=i64(10, 10), offs=i64(0, 4096), n=2, heads=4, dim=64, es=2,
+        bases=two(1 << 20, 1 << 21), world=2, rank=0, flags=8192, phase=0, epoch=1, hs=1, grid=0,
+        status=None, stream=None), **kw).values())
+    for bad, msg in ((dict(n=0), "n_tensors"), (dict(world=17), "world"), (dict(rank=2), "rank"),
+                     (dict(phase=2), "phase"), (dict(dim=4), "16 bytes"), (dict(epoch=0), "epoch"),
+                     (dict(flags=6), "flags_offset"), (dict(offs=i64(0, 8)), "dst_offsets"),
+                     (dict(shards=two(256, 520)), "aligned"), (dict(rows=i64(10, 0)), "rows_local"),
+                     (dict(bases=two(1 << 20, 0)), "rank_bases"), (dict(bases=None), "non-NULL")):
+        assert call(**bad) < 0, bad
+        assert msg in lib.vggt_sparse_last_error().decode(), (bad, lib.vggt_sparse_last_error())
 
 
 def test_token_attention_checks_out_and_status():

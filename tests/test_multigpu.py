@@ -76,6 +76,12 @@ def _worker(rank, world, port, result_q):
             fsb = vd.FrameShardedLayer(16, world, rank, 4, schedule=sched, gather="bulk", **kwc)
             out_b = fsb(x.q[:, s0:s1].contiguous(), *shards)
             ok["frames_bulk_" + sched] = bool(torch.equal(out_b, fullc[:, s0:s1]))
+        # the exchange over NVLink peer memory (two calls: two epochs)
+        fsp = vd.FrameShardedLayer(16, world, rank, 4, gather="push", **kwc)
+        for i in range(2):
+            out_p = fsp(x.q[:, s0:s1].contiguous(), *shards)
+            ok["frames_push_%d" % i] = bool(torch.equal(out_p, fullc[:, s0:s1]))
+        fsp.check_status()
         torch.cuda.synchronize()
         result_q.put((rank, ok))
     except Exception as e:  # report instead of leaving the peer waiting
@@ -100,5 +106,58 @@ def test_two_gpu_shards_match_single_gpu_layer():
     for rank, ok in results.items():
         assert ok == {"qblocks": True, "heads": True, "allgather": True, "frames": True,
                       "frames_groups": True, "frames_bulk_kfirst": True,
-                      "frames_bulk_groups": True}, \
+                      "frames_bulk_groups": True, "frames_push_0": True,
+                      "frames_push_1": True}, \
             (rank, ok)
+
+
+def _push_worker(rank, world, port, result_q):
+    import torch.distributed as dist
+    os.environ["VGGT_ATTN_SPLIT"] = "1"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        import vggt_sparse
+        from vggt_sparse import distributed as vd
+        from vggt_sparse.synthetic import clustered_layer
+        dev = torch.device("cuda", rank)
+        x = clustered_layer(4, centres=64, seed=3, device=dev)
+        kw = dict(mode="mass", tau=0.9, dense_heads=(0, 1))
+        full = vggt_sparse.SparseGlobalLayer(16, **kw)(x.q, x.kp, x.vp, x.ks, x.vs)
+        fs = vd.FrameShardedLayer(16, world, rank, 4, gather="push", **kw)
+        s0, s1 = fs.rows(x.shape.n_tokens)
+        f0, f1 = vd.frame_range(4, world, rank)
+        ppf, spf = 37 * 37, 5
+        shards = [t[:, f0 * ppf:f1 * ppf].contiguous() for t in (x.kp, x.vp)] + \
+                 [t[:, f0 * spf:f1 * spf].contiguous() for t in (x.ks, x.vs)]
+        ok = {}
+        for i in range(3):
+            out = fs(x.q[:, s0:s1].contiguous(), *shards)
+            ok[i] = bool(torch.equal(out, full[:, s0:s1]))
+        kp_full = fs._buffers(shards[0], shards[2])[0]
+        ok["kp"] = bool(torch.equal(kp_full, x.kp))
+        fs.check_status()
+        torch.cuda.synchronize()
+        result_q.put((rank, ok))
+    except Exception as e:  # report instead of leaving the peer waiting
+        result_q.put((rank, {"error": repr(e)}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_push_exchange_on_one_gpu():
+    """The peer-memory exchange with a single rank (its own buffers only):
+    the layer equals the single-GPU layer on three calls in a row."""
+    if torch.cuda.device_count() < 1:
+        pytest.skip("needs a GPU")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_push_worker, args=(0, 1, _free_port(), q))
+    p.start()
+    rank, ok = q.get(timeout=300)
+    p.join(timeout=60)
+    assert ok == {0: True, 1: True, 2: True, "kp": True}, ok
