@@ -63,8 +63,9 @@ def parse_args():
                         "every step; qblocks = query-block shards with the layer's K/V "
                         "replicated on every rank (no collective); heads = each rank holds "
                         "only a cost-balanced set of heads (no collective)")
-    p.add_argument("--gather", choices=("bulk", "heads", "push"), default="bulk",
-                   help="kv-allgather transfer: bulk = one NCCL all-gather per tensor, then a "
+    p.add_argument("--gather", choices=("auto", "bulk", "heads", "push"), default="auto",
+                   help="kv-allgather transfer: auto (default) = push over NCCL process "
+                        "groups; bulk = one NCCL all-gather per tensor, then a "
                         "copy into place; heads = NCCL all-gathers per head; push = this "
                         "library's kernel storing each rank's shards into every rank's "
                         "buffers over NVLink peer memory")
@@ -998,7 +999,7 @@ def main():
         # NCCL head group by head group, overlapped with the groups' compute
         from vggt_sparse import distributed as vd
         runner = vd.FrameShardedLayer(heads, world, rank, cfg.frames, dense_heads=dense,
-                                      gather=args.gather,
+                                      gather=None if args.gather == "auto" else args.gather,
                                       **layer_kwargs)
         f0, f1 = vd.frame_range(cfg.frames, world, rank)
         ppf, spf = x.shape.patch_h * x.shape.patch_w, x.shape.special_per_frame
@@ -1192,7 +1193,7 @@ def main():
                    "tokens": x.shape.n_tokens, "heads": 16, "head_dim": 64,
                    "selection": cfg.mode, "dense_heads": list(cfg.dense_heads),
                    "parallelism": ("%s-sharded x%d%s" % (
-                       args.shard, world, (", %s transfer" % args.gather)
+                       args.shard, world, (", %s transfer" % runner.gather_mode)
                        if args.shard == "kv-allgather" else "")) if world > 1
                    else "single GPU",
                    "l2": "inputs 270 MB > 126 MB L2; 256 MB flush write between timed steps "
@@ -1202,7 +1203,7 @@ def main():
         "kept_block_gflop_per_layer": flops_total / 1e9,
         "frames_per_s": cfg.frames / (ms * 1e-3),
         "estimator_ms": est_local, "attention_ms": att_local,
-        "allgather": ({"what": GATHER_WHAT[args.gather], "alone": gather_alone}
+        "allgather": ({"what": GATHER_WHAT[runner.gather_mode], "alone": gather_alone}
                       if frame_sharded else None),
         "roofline": {"bound": "tensor", "kernel": "block-sparse attention (rank 0)",
                      "achieved": att_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

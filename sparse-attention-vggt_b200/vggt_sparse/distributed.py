@@ -198,6 +198,11 @@ def gather_bulk_async(pairs, h0, h1, world, staging, group=None):
     return _Bulk()
 
 
+def _backend(group):
+    import torch.distributed as dist
+    return dist.get_backend(group) if dist.is_available() and dist.is_initialized() else None
+
+
 class _EventWait:
     """A transfer handle: ``wait()`` orders the current stream after ``event``."""
 
@@ -308,7 +313,8 @@ class FrameShardedLayer:
     takes this rank's query rows ``rows(n_tokens)`` of q and the patch /
     special K/V of its frames ``frame_range`` (every rank the same number of
     frames), and returns this rank's output rows.  K and V are all-gathered
-    over NCCL into head-major buffers: ``gather="bulk"`` (default) moves one
+    into head-major buffers.  The default is ``gather="push"`` for
+    ``schedule="kfirst"`` over NCCL and ``"bulk"`` otherwise.  ``gather="bulk"`` moves one
     all-gather per tensor into rank-major staging and copies it into place;
     ``gather="heads"`` (and any head group that is not a consecutive range)
     moves one all-gather per head and tensor straight into place (more,
@@ -329,11 +335,13 @@ class FrameShardedLayer:
     """
 
     def __init__(self, heads, world, rank, frames, *, dense_heads=(), schedule="kfirst",
-                 groups=None, group=None, gather="bulk", **layer_kwargs):
+                 groups=None, group=None, gather=None, **layer_kwargs):
         if frames % world:
             raise ValueError("frames (%d) must divide evenly over %d ranks" % (frames, world))
         if schedule not in ("kfirst", "groups"):
             raise ValueError("schedule must be 'kfirst' or 'groups'")
+        if gather is None:
+            gather = "push" if schedule == "kfirst" and _backend(group) == "nccl" else "bulk"
         if gather not in ("heads", "bulk", "push"):
             raise ValueError("gather must be 'heads', 'bulk' or 'push'")
         if gather == "push" and schedule != "kfirst":
