@@ -96,6 +96,8 @@ def _work(rank, world, result_q):
     for w in works:
         w.wait()
     gather_ok = gather_ok and all(torch.equal(b, t) for b, t in zip(bufs, (x.kp, x.vp, x.ks, x.vs)))
+    # the transfer a gloo group gets by default: NCCL-free bulk all-gathers
+    gather_ok = gather_ok and vd.FrameShardedLayer(2, world, rank, 4).gather_mode == "bulk"
     # query-block shard of the oracle layer
     n = x.shape.n_tokens
     b0, b1 = vd.qblock_range(-(-n // 64), world, rank)
@@ -122,6 +124,17 @@ def _work(rank, world, result_q):
         result_q.put((gather_ok, float(np.abs(full.numpy() - ref).max())))
     else:
         result_q.put((gather_ok, None))
+
+
+def test_frame_sharded_transfer_choice():
+    """Without an NCCL group the layer moves K/V with bulk all-gathers; the
+    peer-memory exchange runs only with the keys-first schedule."""
+    assert vd.FrameShardedLayer(2, 2, 0, 4).gather_mode == "bulk"
+    assert vd.FrameShardedLayer(2, 2, 0, 4, gather="push").gather_mode == "push"
+    with pytest.raises(ValueError, match="kfirst"):
+        vd.FrameShardedLayer(2, 2, 0, 4, schedule="groups", gather="push")
+    with pytest.raises(ValueError, match="gather must be"):
+        vd.FrameShardedLayer(2, 2, 0, 4, gather="ring")
 
 
 def test_two_rank_gloo_sharding_reassembles_the_layer():
